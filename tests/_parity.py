@@ -1,0 +1,87 @@
+"""Parity checkers shared by the CPU and GPU tests.
+
+The bar (from the project's north star):
+
+* labels are bit-identical except where the two candidate centroids' exact
+  (float64) squared distances differ by less than ``LABEL_TOL[dtype]``
+  relative, and such near-tie mismatches stay under 0.1 % of points;
+* centroids agree within 1e-3 relative per centroid:
+  ``||dc_k|| <= 1e-3 * max(||c_k||, 1e-3 * max_j ||c_j||)``.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import kmeans_oracle as ko
+
+LABEL_TOL = {"float16": 1e-3, "bfloat16": 1e-3, "float32": 1e-5}
+MAX_EXCUSED_FRAC = 1e-3
+CENTROID_RTOL = 1e-3
+
+
+def label_report(x, centroids, got, want, dtype):
+    """Compare two labelings of x against centroids; returns a dict."""
+    got = np.asarray(got).astype(np.int64).reshape(np.asarray(want).shape)
+    want = np.asarray(want).astype(np.int64)
+    mism = got != want
+    n = want.size
+    out = dict(n=n, mismatches=int(mism.sum()), excused=0, bad=0, worst_gap=0.0)
+    if not mism.any():
+        return out
+    x = np.asarray(x, np.float64)
+    c = np.asarray(centroids, np.float64)
+    bi, ni = np.nonzero(mism)
+    xs = x[bi, ni]
+    ca = c[bi, got[bi, ni]]
+    cb = c[bi, want[bi, ni]]
+    da = ((xs - ca) ** 2).sum(-1)
+    db = ((xs - cb) ** 2).sum(-1)
+    gap = np.abs(da - db) / (np.minimum(np.abs(da), np.abs(db)) + 1e-3)
+    tol = LABEL_TOL[dtype]
+    out["excused"] = int((gap < tol).sum())
+    out["bad"] = int((gap >= tol).sum())
+    out["worst_gap"] = float(gap.max())
+    return out
+
+
+def assert_labels(x, centroids, got, want, dtype, what=""):
+    r = label_report(x, centroids, got, want, dtype)
+    assert r["bad"] == 0, f"{what}: {r['bad']} label mismatches beyond near-tie tolerance {r}"
+    assert r["excused"] <= MAX_EXCUSED_FRAC * r["n"], f"{what}: too many near-tie mismatches {r}"
+    return r
+
+
+def centroid_errors(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    nrm = np.linalg.norm(want, axis=-1)
+    floor = 1e-3 * nrm.max(axis=-1, keepdims=True) if nrm.size else nrm
+    denom = np.maximum(nrm, floor)
+    denom = np.where(denom > 0, denom, 1.0)
+    return np.linalg.norm(got - want, axis=-1) / denom
+
+
+def assert_centroids(got, want, what="", rtol=CENTROID_RTOL, skip=None):
+    err = centroid_errors(got, want)
+    if skip is not None:
+        err = np.where(skip, 0.0, err)
+    worst = float(err.max()) if err.size else 0.0
+    assert worst <= rtol, f"{what}: centroid rel error {worst:.3e} > {rtol}"
+    return worst
+
+
+def clusters_touched(labels_a, labels_b, K):
+    """Boolean (B, K): clusters whose membership differs between labelings."""
+    a = np.asarray(labels_a).astype(np.int64)
+    b = np.asarray(labels_b).astype(np.int64)
+    B = a.shape[0]
+    touched = np.zeros((B, K), dtype=bool)
+    for i in range(B):
+        m = a[i] != b[i]
+        touched[i, a[i][m]] = True
+        touched[i, b[i][m]] = True
+    return touched
+
+
+__all__ = ["label_report", "assert_labels", "centroid_errors", "assert_centroids",
+           "clusters_touched", "LABEL_TOL", "ko"]
