@@ -1,0 +1,392 @@
+"""Benchmark of the Lloyd-iteration hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg1|cfg3|cfg4]
+
+A step is one Lloyd iteration (assign + update + shift check) over the whole
+batch of the workload.  Default workload: BASELINE config 2 (B=32, N=75600,
+D=128, K=1000, fp16, x ~ N(0,1)), which fits one GPU.  With N>1 ranks
+(torchrun, NCCL) every rank runs its own replica of the workload (the batched
+path has no exchange step: "replicas only"), and `value` is the aggregate.
+
+`value`: assign-equivalent TFLOP/s = 2*B*N*K*D per iteration / time per
+iteration, whole job.  `e2e`: the same metric through the public API
+(`batch_kmeans_Euclid`, 20 iterations, tol 1e-4) with x copied from pinned host
+memory and the labels/centroids copied back inside each timed step.
+`roofline`: the assignment kernel's own CUDA-event time against the measured
+dense bf16 peak.  `cpu_baseline`: the CPU oracle (numpy restatement of the
+reference's torch path) on a bounded sample, all host cores via a spawn pool.
+`--impl reference`: that CPU oracle alone, timed per step (the reference is a
+Python/Triton package; its CPU path is restated in oracle/).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "flash-kmeans_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "ms/Lloyd iter and assign TFLOP/s (% of peak) at 1/2/4/8 B200 vs host CPU"
+UNIT = "TFLOP/s"
+
+WORKLOADS = {
+    "cfg1": dict(B=2, N=16384, D=128, K=256, dtype="float32", gen="gmm", comps=256, mean_std=2.0),
+    "cfg2": dict(B=32, N=75600, D=128, K=1000, dtype="float16", gen="randn"),
+    "cfg3": dict(B=1, N=1 << 22, D=128, K=128, dtype="float16", gen="gmm", comps=128,
+                 mean_std=3.0, dirichlet=True),
+    "cfg4": dict(B=1, N=262144, D=2048, K=1024, dtype="float32", gen="randn"),
+}
+
+
+def _flops(w):
+    return 2.0 * w["B"] * w["N"] * w["K"] * w["D"]
+
+
+def _describe(name, w):
+    return (f"{name}: B={w['B']} N={w['N']} D={w['D']} K={w['K']} {w['dtype']}, "
+            + ("x~N(0,1)" if w["gen"] == "randn" else f"GMM({w['comps']} comps)"))
+
+
+# ----------------------------------------------------------------- CPU oracle
+def _oracle_batch_iter(args):
+    """One Lloyd iteration of the numpy oracle on one batch (runs in a worker)."""
+    seed, N, K, D, dtype = args
+    import numpy as np
+    from oracle import kmeans_oracle as ko
+    rng = np.random.default_rng(seed)
+    x = ko.round_to(rng.standard_normal((1, N, D), dtype=np.float32), dtype)
+    c = ko.init_from_points(rng, x, K, replace=True)
+    t0 = time.perf_counter()
+    x_sq = ko.row_sqnorm(x, dtype)
+    ko.lloyd_iter(x, x_sq, c, dtype, exact_order=False)
+    return time.perf_counter() - t0
+
+
+class CpuOracle:
+    """Spawned pool; each step runs one Lloyd iteration on `batches` batches."""
+
+    def __init__(self, w):
+        import multiprocessing as mp
+        os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+        os.environ.setdefault("OMP_NUM_THREADS", "1")
+        self.w = w
+        self.cores = max(1, min(os.cpu_count() or 1, 16, w["B"]))
+        self.pool = mp.get_context("spawn").Pool(self.cores)
+
+    def step(self, seed=0):
+        w = self.w
+        jobs = [(seed * 1000 + i, w["N"], w["K"], w["D"], w["dtype"]) for i in range(self.cores)]
+        t0 = time.perf_counter()
+        self.pool.map(_oracle_batch_iter, jobs)
+        return time.perf_counter() - t0
+
+    def tflops(self, seconds):
+        return _flops(self.w) / self.w["B"] * self.cores / seconds / 1e12
+
+    def sample(self):
+        return (f"{self.cores} of {self.w['B']} batches of the workload, one Lloyd iteration "
+                f"per step (numpy oracle, one process per core)")
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+# -------------------------------------------------------------- clock sampler
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting"}
+
+    def __init__(self, torch_device, period_s=0.005):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.power_w = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # sampling is best effort; the JSON says so
+            self.error = repr(e)
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.power_w.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz,
+                "reasons": [n for b, n in self.REASONS.items() if self.reasons & b],
+                "samples": len(self.samples),
+                "power_w_max": max(self.power_w) if self.power_w else None}
+
+
+# ----------------------------------------------------------------- our arm
+def _make_inputs(w, device, seed=0):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, N, D, K = w["B"], w["N"], w["D"], w["K"]
+    dt = getattr(torch, w["dtype"])
+    if w["gen"] == "randn":
+        x = torch.randn((B, N, D), device=device, generator=g, dtype=torch.float32)
+    else:
+        means = torch.randn((B, w["comps"], D), device=device, generator=g) * w["mean_std"]
+        if w.get("dirichlet"):
+            wts = torch.distributions.Dirichlet(torch.ones(w["comps"])).sample((B,)).to(device)
+        else:
+            wts = torch.full((B, w["comps"]), 1.0 / w["comps"], device=device)
+        comp = torch.multinomial(wts, N, replacement=True, generator=g)
+        x = torch.gather(means, 1, comp[..., None].expand(-1, -1, D))
+        x += torch.randn((B, N, D), device=device, generator=g)
+    x = x.to(dt)
+    idx = torch.randint(0, N, (B, K), device=device, generator=g)
+    c0 = torch.gather(x, 1, idx[..., None].expand(-1, -1, D)).contiguous()
+    return x, c0
+
+
+def _load_traffic(name):
+    path = os.path.join(ROOT, "profiles", f"assign_{name}_ncu.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p.get("bf16_tflops_sustained"), p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from flash_kmeans import batch_kmeans_Euclid
+    from flash_kmeans.kmeans_triton_impl import LloydEngine
+
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, N, D, K = w["B"], w["N"], w["D"], w["K"]
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuOracle(w)  # spawn before heavy GPU work
+
+    x, c0 = _make_inputs(w, dev, seed=1234 + rank)
+    eng = LloydEngine(B, N, K, D, x.dtype, dev)
+    eng.load(x, c0)
+    torch.cuda.synchronize()
+
+    steps, warm = args.steps, args.warmup
+    a0 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    a1 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+
+    def one_step(i=None):
+        eng.step(ev_assign=(a0[i], a1[i]) if i is not None else None)
+        shift, code = eng.read_stat()   # the reference's per-iteration `shift < tol` check
+        if code:
+            raise RuntimeError(f"device status {code}")
+        eng.advance()
+
+    for _ in range(warm):
+        one_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for i in range(steps):
+            one_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    assign_ms = sum(a0[i].elapsed_time(a1[i]) for i in range(steps)) / steps
+    t = torch.tensor([ms, assign_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, assign_ms = float(t[0]), float(t[1])
+
+    flops = _flops(w)
+    value = flops * world / (ms * 1e-3) / 1e12
+    burst, sustained, hbm, src = _peaks()
+    achieved = flops / (assign_ms * 1e-3) / 1e12
+
+    # ---- e2e through the public API with host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        x_h = x.cpu().pin_memory()
+        c_h = c0.cpu().pin_memory()
+        del x
+        torch.cuda.empty_cache()
+        iters_total, t_total = 0, 0.0
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        for s in range(args.e2e_steps + 1):
+            torch.cuda.synchronize()
+            f0.record()
+            xd = x_h.to(dev, non_blocking=True)
+            cd = c_h.to(dev, non_blocking=True)
+            ids, cent, n_it = batch_kmeans_Euclid(xd, K, max_iters=20, tol=1e-4, init_centroids=cd)
+            ids_h = ids.to("cpu")
+            cent_h = cent.to("cpu")
+            f1.record()
+            torch.cuda.synchronize()
+            if s > 0:  # first run is warm-up
+                iters_total += n_it
+                t_total += f0.elapsed_time(f1) * 1e-3
+            del xd, cd, ids, cent
+        tt = torch.tensor([t_total], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(flops * iters_total / args.e2e_steps * world
+                              / (float(tt[0]) / args.e2e_steps) / 1e12, 3),
+               "unit": UNIT,
+               "h2d_bytes_per_step": int(x_h.numel() * x_h.element_size()
+                                         + c_h.numel() * c_h.element_size()),
+               "d2h_bytes_per_step": int(ids_h.numel() * 4 + cent_h.numel() * cent_h.element_size()),
+               "step": "batch_kmeans_Euclid(max_iters=20, tol=1e-4) on x copied from pinned host, "
+                       "labels+centroids copied back",
+               "iters_per_step": iters_total / args.e2e_steps}
+
+    cpu_baseline = None
+    if cpu is not None:
+        cpu.step(seed=99)                      # warm the workers (imports, allocation)
+        secs = cpu.step(seed=7)
+        cpu_baseline = {"value": round(cpu.tflops(secs), 5), "unit": UNIT, "cores": cpu.cores,
+                        "kind": "port", "sample": cpu.sample()}
+        cpu.close()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16" if w["dtype"] == "float16" else ("bf16" if w["dtype"] == "bfloat16" else "f32(3xTF32)"),
+            "data": "synthetic (seeded torch generator; shapes/distribution of the BASELINE config)",
+            "config": {"workload": _describe(args.workload, w),
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs exceed the 126 MB L2 (x is %d MB); no flush" %
+                             (B * N * D * (2 if w["dtype"] != "float32" else 4) // 2 ** 20),
+                       "step": "one Lloyd iteration incl. the per-iteration shift readback"},
+            "ms_per_iter": round(ms, 4),
+            "assign_ms": round(assign_ms, 4),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst,
+                         "unit": UNIT, "frac": round(achieved / burst, 4),
+                         "peak_source": f"{src} dense bf16 (burst)",
+                         "frac_of_sustained": round(achieved / sustained, 4) if sustained else None,
+                         "traffic": _load_traffic(args.workload)},
+            "e2e": e2e,
+            "cpu_baseline": cpu_baseline,
+            "gpu_launches": 6 * steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    cpu = CpuOracle(w)
+    for s in range(args.warmup):
+        cpu.step(seed=s)
+    times = [cpu.step(seed=100 + s) for s in range(args.steps)]
+    cpu.close()
+    secs = sum(times) / len(times)
+    v = round(cpu.tflops(secs), 5)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": v, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": w["dtype"], "data": "synthetic",
+        "config": {"workload": _describe(args.workload, w)},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu.cores, "kind": "port",
+                         "sample": cpu.sample()},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,727 @@
+// Nearest-centroid assignment on sm_100a (replaces _euclid_assign_kernel and
+// _euclid_assign_kernel_split_d, flash_kmeans/assign_euclid_triton.py:804-1030).
+//
+// One persistent CTA per SM walks (batch, 128-point tile) work items.  Per
+// item it streams the batch's centroids in tiles of 256 through a TMA ring and
+// computes the 128 x 256 cross products x.c^T with tcgen05.mma into one of
+// two TMEM accumulators (2 x 256 of the 512 columns), so the epilogue of tile
+// j overlaps the MMAs of tile j+1.  The epilogue reads its TMEM lane (= its
+// point) with tcgen05.ld, forms the distance with the reference torch path's
+// rounding and keeps a running argmin; the (B,N,K) distance matrix never
+// exists.  Nothing is written but one int32 label per point (and, optionally,
+// +1 on that label's count).
+//
+// Roles (warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
+// 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4).. and half (w-2)/4 of
+// each 256-column tile), 10..13 = f32 split converters (3xTF32 mode only).
+//
+// Modes:
+//   0  16-bit x with x_sq in the same dtype: dist = r(r(x_sq - 2 r(x.c)) + c_sq),
+//      r = round to that dtype, evaluated two columns at a time on packed
+//      half2 / bfloat162 registers.  This is the reference torch path's op
+//      chain (torch_fallback.py:41-45) with no clamp.
+//   1  16-bit x, float32 x_sq: cross rounded to the 16-bit dtype (the bmm output
+//      dtype), then the float32 chain (type promotion of torch_fallback.py:41-45).
+//   2  float32 x: cross = 3xTF32 (hi*hi + hi*lo + lo*hi, hi = tf32-rounded
+//      value, lo = exact remainder, split in shared memory by warps 10..13),
+//      float32 chain.
+// Split-D: when the x tile (128 points x D) does not fit twice in shared
+// memory (more than two 128-byte column chunks) the x chunk travels with each
+// centroid chunk instead of staying resident.
+#include "fk_common.cuh"
+#include "fk_ptx.cuh"
+
+namespace fk {
+
+constexpr int kRows = 128;            // points per tile (MMA M)
+constexpr int kCent = 256;            // centroids per tile (MMA N)
+constexpr int kChunkB = 128;          // bytes per row chunk = one 128B swizzle span
+constexpr int kXChunk = kRows * kChunkB;   // 16 KB
+constexpr int kCChunk = kCent * kChunkB;   // 32 KB
+constexpr int kEpiWarps = 8;
+constexpr int kEpiWarp0 = 2;
+constexpr int kConvWarp0 = 10;
+constexpr int kConvWarps = 4;
+constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
+
+template <int MODE, bool XRES, int STAGES>
+struct Layout {
+  static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
+  static constexpr int x_off = 0;
+  static constexpr int x_bytes = XRES ? 2 * kResidentChunks * kXChunk : 0;
+  static constexpr int st_c = 0;                          // centroid chunk (hi)
+  static constexpr int st_clo = kCChunk;                  // centroid chunk lo (mode 2)
+  static constexpr int st_x = kCChunk * kSplit;           // x chunk (split-D)
+  static constexpr int st_xlo = st_x + kXChunk;           // x chunk lo (mode 2)
+  static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
+  static constexpr int stages_off = x_off + x_bytes;
+  static constexpr int merge_off = stages_off + STAGES * stage_bytes;
+  static constexpr int merge_bytes = 2 * kRows * 8;     // [parity][row] (value, index)
+  static constexpr int bar_off = merge_off + merge_bytes;
+  // x_full[2] x_empty[2] c_full[S] c_empty[S] conv_full[S] acc_full[2] acc_empty[2]
+  // merge_full[2] merge_empty[2] final[1]
+  static constexpr int nbars = 4 + 3 * STAGES + 4 + 4 + 1;
+  static constexpr int misc_off = bar_off + nbars * 8;
+  static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
+  static constexpr int threads = (MODE == 2 ? 14 : 10) * 32;
+};
+
+struct AssignParams {
+  const void* xsq;
+  int64_t sxq_b, sxq_n;
+  int xsq_dtype;
+  const void* csq;  // (B, Kpad) in the distance dtype, +inf beyond K
+  int64_t kpad;
+  int32_t* out;
+  int64_t so_b, so_n;
+  int32_t* counts;  // (B, K) or null
+  int N, K;
+  int nd;           // 128-byte column chunks per row
+  int dch;          // elements per chunk
+  int ntn;          // point tiles per batch
+  int nkt;          // centroid tiles
+  int total_tiles;
+  int* status;
+};
+
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- epilogue math
+// Packed 16-bit helpers (mode 0).
+template <typename T>
+struct Pack2;
+
+template <>
+struct Pack2<__half> {
+  using V = __half2;
+  static constexpr uint32_t kInf2 = 0x7C007C00u;
+  __device__ __forceinline__ static uint32_t dist(float c0, float c1, uint32_t xsq2, uint32_t csq2) {
+    const __half2 cr = __floats2half2_rn(c0, c1);  // .x = even column
+    const __half2 neg2 = __float2half2_rn(-2.0f);
+    const __half2 t = __hfma2(cr, neg2, *reinterpret_cast<const __half2*>(&xsq2));
+    const __half2 d = __hadd2(t, *reinterpret_cast<const __half2*>(&csq2));
+    return *reinterpret_cast<const uint32_t*>(&d);
+  }
+  __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
+    return __hlt2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  }
+  __device__ __forceinline__ static float lo(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+  }
+  __device__ __forceinline__ static float hi(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+  }
+  __device__ __forceinline__ static uint32_t splat(float v) {
+    const __half2 h = __float2half2_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+
+template <>
+struct Pack2<__nv_bfloat16> {
+  using V = __nv_bfloat162;
+  static constexpr uint32_t kInf2 = 0x7F807F80u;
+  __device__ __forceinline__ static uint32_t dist(float c0, float c1, uint32_t xsq2, uint32_t csq2) {
+    const __nv_bfloat162 cr = __floats2bfloat162_rn(c0, c1);
+    const __nv_bfloat162 neg2 = __float2bfloat162_rn(-2.0f);
+    const __nv_bfloat162 t = __hfma2(cr, neg2, *reinterpret_cast<const __nv_bfloat162*>(&xsq2));
+    const __nv_bfloat162 d = __hadd2(t, *reinterpret_cast<const __nv_bfloat162*>(&csq2));
+    return *reinterpret_cast<const uint32_t*>(&d);
+  }
+  __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
+    return __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+  }
+  __device__ __forceinline__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
+  __device__ __forceinline__ static float hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+  __device__ __forceinline__ static uint32_t splat(float v) {
+    const __nv_bfloat162 h = __float2bfloat162_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+
+// Round a float to the 16-bit type and back (mode 1 cross rounding).
+template <typename T>
+__device__ __forceinline__ float round16(float v) {
+  return Elem<T>::round(v);
+}
+
+// --------------------------------------------------------------------- kernel
+template <typename T, int MODE, bool XRES, int STAGES>
+__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
+    assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                  const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
+  using L = Layout<MODE, XRES, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar_off);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = bars + 2;
+  uint64_t* c_full = bars + 4;
+  uint64_t* c_empty = c_full + STAGES;
+  uint64_t* conv_full = c_empty + STAGES;
+  uint64_t* acc_full = conv_full + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* merge_full = acc_empty + 2;
+  uint64_t* merge_empty = merge_full + 2;
+  uint64_t* final_bar = merge_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps * 32);
+      mbar_init(&merge_full[i], 4 * 32);
+      mbar_init(&merge_empty[i], 4 * 32);
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&c_full[s], 1);
+      mbar_init(&c_empty[s], 1);
+      mbar_init(&conv_full[s], kConvWarps * 32);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_c);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t sph = 0;
+      int xb = 0;
+      uint32_t xph = 0;
+      int last_par[STAGES];
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      int last_xpar[2] = {-1, -1};
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const int b = t / p.ntn;
+        const int row0 = (t % p.ntn) * kRows;
+        if constexpr (XRES) {
+          if (!mbar_wait(&x_empty[xb], xph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&x_full[xb], p.nd * kXChunk);
+          for (int dc = 0; dc < p.nd; ++dc)
+            tma_load_3d(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk, &tmap_x,
+                        &x_full[xb], dc * p.dch, row0, b);
+          last_xpar[xb] = static_cast<int>(xph);
+          if (++xb == 2) { xb = 0; xph ^= 1; }
+        }
+        for (int kt = 0; ok && kt < p.nkt; ++kt) {
+          for (int dc = 0; dc < p.nd; ++dc) {
+            if (!mbar_wait(&c_empty[stage], sph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
+            mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : kXChunk));
+            tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
+            if constexpr (!XRES)
+              tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
+            last_par[stage] = static_cast<int>(sph);
+            if (++stage == STAGES) { stage = 0; sph ^= 1; }
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load already issued land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) drain_wait(&c_full[s], static_cast<uint32_t>(last_par[s]), 200000000ull);
+        for (int i = 0; i < 2; ++i)
+          if (last_xpar[i] >= 0) drain_wait(&x_full[i], static_cast<uint32_t>(last_xpar[i]), 200000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(Elem<T>::kMmaFmt, kRows, kCent);
+      int stage = 0;
+      uint32_t sph = 0;
+      int xb = 0;
+      uint32_t xph = 0;
+      int ab = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        if constexpr (XRES) {
+          if (!mbar_wait(&x_full[xb], xph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        for (int kt = 0; ok && kt < p.nkt; ++kt) {
+          if (!mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
+          for (int dc = 0; dc < p.nd; ++dc) {
+            uint64_t* ready = (MODE == 2) ? &conv_full[stage] : &c_full[stage];
+            if (!mbar_wait(ready, sph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
+            const uint32_t a_addr =
+                XRES ? smem_u32(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk)
+                     : smem_u32(st + L::st_x);
+            const uint32_t b_addr = smem_u32(st + L::st_c);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint32_t acc = (dc > 0 || ks > 0) ? 1u : 0u;
+              const uint32_t off = static_cast<uint32_t>(ks * 32);
+              if constexpr (MODE == 2) {
+                const uint32_t alo = smem_u32(st + L::st_xlo);
+                const uint32_t blo = smem_u32(st + L::st_clo);
+                mma_tf32(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off),
+                         idesc, acc);
+                mma_tf32(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(blo + off), idesc,
+                         1u);
+                mma_tf32(d_tmem, smem_desc_sw128(alo + off), smem_desc_sw128(b_addr + off), idesc,
+                         1u);
+              } else {
+                mma_f16(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off),
+                        idesc, acc);
+              }
+            }
+            mma_commit(&c_empty[stage]);
+            if (++stage == STAGES) { stage = 0; sph ^= 1; }
+          }
+          if (!ok) break;
+          mma_commit(&acc_full[ab]);
+          if (++ab == 2) { ab = 0; aph ^= 1; }
+        }
+        if constexpr (XRES) {
+          if (ok) {
+            mma_commit(&x_empty[xb]);
+            if (++xb == 2) { xb = 0; xph ^= 1; }
+          }
+        }
+      }
+      // All MMAs this thread issued must finish before TMEM is released.
+      mma_commit(final_bar);
+      drain_wait(final_bar, 0, 1000000000ull);
+    }
+  } else if (warp < kEpiWarp0 + kEpiWarps) {
+    // ------------------------------------------------------------- epilogue
+    const int ew = warp - kEpiWarp0;
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int h = ew >> 2;           // which 128-column half of each tile
+    const int row = q * 32 + lane;   // point within the tile
+    uint2* merge = reinterpret_cast<uint2*>(smem + L::merge_off);
+    int ab = 0;
+    uint32_t aph = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++it) {
+      const int b = t / p.ntn;
+      const int n = (t % p.ntn) * kRows + row;
+      const bool valid = n < p.N;
+      const float xsq_f = valid ? load_f(p.xsq, b * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
+
+      uint32_t best2 = 0, bloc = 0, bchunk = 0;  // mode 0 state
+      float bestf = __int_as_float(0x7f800000);  // modes 1/2 state
+      int bl = 0, bch = 0;
+      uint32_t xsq2 = 0;
+      if constexpr (MODE == 0) {
+        best2 = Pack2<T>::kInf2;
+        xsq2 = Pack2<T>::splat(xsq_f);  // exact: x_sq already holds a T value
+      }
+      const uint8_t* csq_row =
+          static_cast<const uint8_t*>(p.csq) +
+          static_cast<size_t>(b) * p.kpad * (MODE == 0 ? 2 : 4);
+
+      for (int kt = 0; kt < p.nkt; ++kt) {
+        // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+        const bool got = mbar_wait(&acc_full[ab], aph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               static_cast<uint32_t>(ab * kCent + h * 128);
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          const int col0 = kt * kCent + h * 128 + ch * 32;
+          uint32_t v[32];
+          tmem_ld32(tbase + ch * 32, v);
+          if constexpr (MODE == 0) {
+            const uint4* cq = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
+            uint4 c4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c4[i] = __ldg(cq + i);
+            tmem_ld_wait(v);
+            const uint32_t* cw = reinterpret_cast<const uint32_t*>(c4);
+            const uint32_t prev = best2;
+#pragma unroll
+            for (int pp = 0; pp < 16; ++pp) {
+              const uint32_t d = Pack2<T>::dist(__uint_as_float(v[2 * pp]),
+                                                __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
+              const uint32_t m = Pack2<T>::lt_mask(d, best2);
+              best2 = (d & m) | (best2 & ~m);
+              bloc = ((static_cast<uint32_t>(pp) * 0x00010001u) & m) | (bloc & ~m);
+            }
+            const uint32_t chg = __vcmpne2(best2, prev);
+            const uint32_t cid2 = static_cast<uint32_t>(col0 >> 5) * 0x00010001u;
+            bchunk = (cid2 & chg) | (bchunk & ~chg);
+          } else {
+            const float4* cq = reinterpret_cast<const float4*>(csq_row + col0 * 4);
+            float4 c4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c4[i] = __ldg(cq + i);
+            tmem_ld_wait(v);
+            const float* cs = reinterpret_cast<const float*>(c4);
+            const float prev = bestf;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float cr = __uint_as_float(v[j]);
+              if constexpr (MODE == 1) cr = round16<T>(cr);
+              const float tt = __fmaf_rn(-2.0f, cr, xsq_f);
+              const float d = __fadd_rn(tt, cs[j]);
+              const bool lt = d < bestf;
+              bestf = lt ? d : bestf;
+              bl = lt ? j : bl;
+            }
+            bch = (bestf != prev) ? (col0 >> 5) : bch;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[ab]);
+        if (++ab == 2) { ab = 0; aph ^= 1; }
+      }
+      if (!ok) break;
+
+      // Per-thread winner: (value, lowest column on ties).
+      float val;
+      int idx;
+      if constexpr (MODE == 0) {
+        const float ve = Pack2<T>::lo(best2), vo = Pack2<T>::hi(best2);
+        const int ie = static_cast<int>(((bchunk & 0xFFFFu) << 5) + ((bloc & 0xFFFFu) << 1));
+        const int io = static_cast<int>(((bchunk >> 16) << 5) + ((bloc >> 16) << 1) + 1);
+        const bool take_odd = (vo < ve) || (vo == ve && io < ie);
+        val = take_odd ? vo : ve;
+        idx = take_odd ? io : ie;
+      } else {
+        val = bestf;
+        idx = (bch << 5) + bl;
+      }
+
+      // Merge the two column halves: half 1 publishes, half 0 decides.
+      const int par = it & 1;
+      const uint32_t mph = static_cast<uint32_t>((it >> 1) & 1);
+      uint2* slot = merge + par * kRows + row;
+      if (h == 1) {
+        const bool got = mbar_wait(&merge_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        *slot = make_uint2(__float_as_uint(val), static_cast<uint32_t>(idx));
+        mbar_arrive(&merge_full[par]);
+      } else {
+        const bool got = mbar_wait(&merge_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint2 o = *slot;
+        mbar_arrive(&merge_empty[par]);
+        const float vo = __uint_as_float(o.x);
+        const int io = static_cast<int>(o.y);
+        if (vo < val || (vo == val && io < idx)) {
+          val = vo;
+          idx = io;
+        }
+        if (valid) {
+          p.out[b * p.so_b + static_cast<int64_t>(n) * p.so_n] = idx;
+          if (p.counts) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
+        }
+      }
+    }
+  } else if (MODE == 2) {
+    // ---------------------------------------- 3xTF32 split converters (mode 2)
+    const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
+    int stage = 0;
+    uint32_t sph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int kt = 0; ok && kt < p.nkt; ++kt) {
+        for (int dc = 0; dc < p.nd; ++dc) {
+          const bool got = mbar_wait(&c_full[stage], sph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
+          // hi = value rounded to tf32 (10 explicit mantissa bits), lo = exact rest
+          auto split = [&](int hi_off, int lo_off, int nfloat4) {
+            float4* hi = reinterpret_cast<float4*>(st + hi_off);
+            float4* lo = reinterpret_cast<float4*>(st + lo_off);
+            for (int i = ct; i < nfloat4; i += kConvWarps * 32) {
+              float4 v = hi[i];
+              float4 vh, vl;
+              uint32_t u;
+              u = (__float_as_uint(v.x) + 0x1000u) & 0xFFFFE000u; vh.x = __uint_as_float(u); vl.x = v.x - vh.x;
+              u = (__float_as_uint(v.y) + 0x1000u) & 0xFFFFE000u; vh.y = __uint_as_float(u); vl.y = v.y - vh.y;
+              u = (__float_as_uint(v.z) + 0x1000u) & 0xFFFFE000u; vh.z = __uint_as_float(u); vl.z = v.z - vh.z;
+              u = (__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u; vh.w = __uint_as_float(u); vl.w = v.w - vh.w;
+              hi[i] = vh;
+              lo[i] = vl;
+            }
+          };
+          split(L::st_c, L::st_clo, kCChunk / 16);
+          split(L::st_x, L::st_xlo, kXChunk / 16);
+          fence_proxy_async_smem();
+          mbar_arrive(&conv_full[stage]);
+          if (++stage == STAGES) { stage = 0; sph ^= 1; }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+template <typename T, int MODE, bool XRES>
+static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
+                         cudaStream_t stream) {
+  constexpr int STAGES = (MODE == 2) ? 2 : 4;
+  using L = Layout<MODE, XRES, STAGES>;
+  static_assert(L::total <= 232448, "shared memory budget");
+  auto kern = assign_kernel<T, MODE, XRES, STAGES>;
+  const int dev = current_device();
+  static bool attr_set[64] = {false};
+  if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const int sms = sm_count_current();
+  if (sms <= 0) return fail(FK_ERR_CUDA, "could not query SM count");
+  const int grid = p.total_tiles < sms ? p.total_tiles : sms;
+  kern<<<grid, L::threads, L::total, stream>>>(tx, tc, p);
+  return check_launch("assign_kernel");
+}
+
+// Padded per-centroid squared norms in the epilogue's distance dtype.
+// Modes 0/1 follow (c ** 2).sum(-1) in the 16-bit dtype (torch_fallback.py:23);
+// mode 2 in float32.  A caller-provided c_sq is converted instead.
+template <typename T, int MODE>
+__global__ void prep_csq_kernel(const T* __restrict__ c, int64_t scb, int64_t sck, int64_t scd,
+                                const void* csq_in, int csq_dtype, int64_t sqb, int64_t sqk,
+                                void* csq_out, int64_t kpad, int B, int K, int D) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t total = static_cast<int64_t>(B) * kpad;
+  for (int64_t r = gw; r < total; r += static_cast<int64_t>(gridDim.x) * warps_per_block) {
+    const int b = static_cast<int>(r / kpad);
+    const int k = static_cast<int>(r % kpad);
+    float v;
+    if (k >= K) {
+      v = __int_as_float(0x7f800000);
+    } else if (csq_in) {
+      v = load_f(csq_in, b * sqb + k * sqk, csq_dtype);
+    } else {
+      const T* row = c + b * scb + k * sck;
+      float acc = 0.0f;
+      for (int d = lane; d < D; d += 32) {
+        const float e = Elem<T>::to_f(row[d * scd]);
+        acc += (MODE == 2) ? e * e : Elem<T>::round(e * e);
+      }
+      acc = warp_sum(acc);
+      v = (MODE == 2) ? acc : Elem<T>::round(acc);
+    }
+    if (lane == 0) {
+      if (MODE == 0)
+        static_cast<T*>(csq_out)[r] = Elem<T>::from_f(v);
+      else
+        static_cast<float*>(csq_out)[r] = v;
+    }
+  }
+}
+
+template <typename T>
+static int assign_typed(const void* x, const void* cent, const void* x_sq, const void* c_sq,
+                        int32_t* out, int32_t* counts, int xsq_dtype, int csq_dtype, int64_t B,
+                        int64_t N, int64_t K, int64_t D, const int64_t* xs, const int64_t* cs,
+                        const int64_t* xqs, const int64_t* cqs, const int64_t* os, void* ws,
+                        int32_t* status, cudaStream_t stream) {
+  constexpr int eb = Elem<T>::kBytes;
+  const bool is16 = eb == 2;
+  const int mode = is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2;
+  const int dch = kChunkB / eb;
+  const int nd = static_cast<int>((D + dch - 1) / dch);
+  const int nkt = static_cast<int>((K + kCent - 1) / kCent);
+  const int64_t kpad = static_cast<int64_t>(nkt) * kCent;
+  const bool xres = is16 && nd <= kResidentChunks;
+
+  // 1) padded c_sq in the distance dtype
+  {
+    const int threads = 256;
+    const int64_t rows = B * kpad;
+    const int blocks = static_cast<int>(rows / 8 + 1 < 4096 ? rows / 8 + 1 : 4096);
+    const T* c = static_cast<const T*>(cent);
+    if (mode == 0)
+      prep_csq_kernel<T, 0><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
+          (int)B, (int)K, (int)D);
+    else if (mode == 1)
+      prep_csq_kernel<T, 1><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
+          (int)B, (int)K, (int)D);
+    else
+      prep_csq_kernel<T, 2><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
+          (int)B, (int)K, (int)D);
+    int st = check_launch("prep_csq_kernel");
+    if (st != FK_OK) return st;
+  }
+
+  // 2) tensor maps: x as (D, N, B), centroids as (D, K, B), 128-byte swizzle
+  CUtensorMap tx, tc;
+  int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows);
+  if (st != FK_OK) return st;
+  st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kCent);
+  if (st != FK_OK) return st;
+
+  AssignParams p;
+  p.xsq = x_sq;
+  p.sxq_b = xqs[0];
+  p.sxq_n = xqs[1];
+  p.xsq_dtype = xsq_dtype;
+  p.csq = ws;
+  p.kpad = kpad;
+  p.out = out;
+  p.so_b = os[0];
+  p.so_n = os[1];
+  p.counts = counts;
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.nd = nd;
+  p.dch = dch;
+  p.ntn = static_cast<int>((N + kRows - 1) / kRows);
+  p.nkt = nkt;
+  p.total_tiles = static_cast<int>(B * p.ntn);
+  p.status = status;
+
+  if constexpr (Elem<T>::kBytes == 2) {
+    if (mode == 0) return xres ? launch_assign<T, 0, true>(tx, tc, p, stream)
+                               : launch_assign<T, 0, false>(tx, tc, p, stream);
+    return xres ? launch_assign<T, 1, true>(tx, tc, p, stream)
+                : launch_assign<T, 1, false>(tx, tc, p, stream);
+  } else {
+    return launch_assign<T, 2, false>(tx, tc, p, stream);
+  }
+}
+
+}  // namespace fk
+
+using namespace fk;
+
+extern "C" size_t fk_assign_workspace_size(int64_t B, int64_t K, int dtype) {
+  (void)dtype;
+  if (B <= 0 || K <= 0) return 256;
+  const int64_t kpad = (K + kCent - 1) / kCent * kCent;
+  return align_up(static_cast<size_t>(B * kpad * 4), 256) + 256;
+}
+
+extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
+                         int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,
+                         int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
+                         const int64_t* c_strides3, const int64_t* xsq_strides2,
+                         const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
+                         size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (B < 0 || N < 0 || K <= 0 || D <= 0)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign: bad sizes B=%lld N=%lld K=%lld D=%lld",
+                (long long)B, (long long)N, (long long)K, (long long)D);
+  if (B == 0 || N == 0) return FK_OK;
+  if (!x || !centroids || !x_sq || !out || !x_strides3 || !c_strides3 || !xsq_strides2 ||
+      !out_strides2)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign: null pointer argument");
+  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "fk_assign: c_sq without strides");
+  if (dtype != FK_F16 && dtype != FK_BF16 && dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign: x dtype must be f16, bf16 or f32");
+  if (xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign: x_sq dtype must be floating");
+  if (c_sq && csq_dtype != FK_F16 && csq_dtype != FK_BF16 && csq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign: c_sq dtype must be floating");
+  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "fk_assign: K=%lld above 2^20", (long long)K);
+  if (N >= (1ll << 31) || B * ((N + kRows - 1) / kRows) >= (1ll << 31))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign: problem too large for 32-bit tile indices");
+  // Strides of size-1 dimensions are irrelevant; give TMA valid ones.
+  const int64_t eb = dtype == FK_F32 ? 4 : 2;
+  const int64_t row_al = 16 / eb;
+  int64_t xs[3] = {x_strides3[0], x_strides3[1], x_strides3[2]};
+  int64_t cs[3] = {c_strides3[0], c_strides3[1], c_strides3[2]};
+  if (D == 1) { xs[2] = 1; cs[2] = 1; }
+  if (N == 1) xs[1] = (D + row_al - 1) / row_al * row_al;
+  if (K == 1) cs[1] = (D + row_al - 1) / row_al * row_al;
+  if (B == 1) { xs[0] = N * xs[1]; cs[0] = K * cs[1]; }
+  x_strides3 = xs;
+  c_strides3 = cs;
+  if (!fk_tma_compatible(x, dtype, D, x_strides3))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign: x rows not TMA-addressable (pack with fk_pack_rows)");
+  if (!fk_tma_compatible(centroids, dtype, D, c_strides3))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign: centroid rows not TMA-addressable");
+  const size_t need = fk_assign_workspace_size(B, K, dtype);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FK_ERR_WORKSPACE, "fk_assign: workspace needs %zu bytes, 256-aligned", need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case FK_F16:
+      return assign_typed<__half>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N,
+                                  K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
+                                  out_strides2, workspace, dev_status, s);
+    case FK_BF16:
+      return assign_typed<__nv_bfloat16>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype,
+                                         csq_dtype, B, N, K, D, x_strides3, c_strides3,
+                                         xsq_strides2, csq_strides2, out_strides2, workspace,
+                                         dev_status, s);
+    default:
+      return assign_typed<float>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N,
+                                 K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
+                                 out_strides2, workspace, dev_status, s);
+  }
+}

@@ -1,0 +1,130 @@
+// Per-row squared norms (x_sq, kmeans_triton_impl.py:84-87) and row packing.
+#include "fk_common.cuh"
+
+namespace fk {
+
+// One warp per row.  Same-dtype output follows `(x ** 2).sum(-1)` in that
+// dtype: each square rounded to the dtype, float32 accumulation, one final
+// rounding.  Float32 output squares and sums in float32.
+template <typename T, bool SAME>
+__global__ void row_sqnorm_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
+                                  void* out, int out_dtype, int64_t sob, int64_t son, int N,
+                                  int D, int64_t rows) {
+  const int wpb = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); r < rows;
+       r += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t b = r / N;
+    const int64_t n = r % N;
+    const T* row = x + b * sxb + n * sxn;
+    float acc = 0.0f;
+    if (sxd == 1) {
+#pragma unroll 4
+      for (int d = lane; d < D; d += 32) {
+        const float e = Elem<T>::to_f(row[d]);
+        acc += SAME ? Elem<T>::round(e * e) : e * e;
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) {
+        const float e = Elem<T>::to_f(row[d * sxd]);
+        acc += SAME ? Elem<T>::round(e * e) : e * e;
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) store_f(out, b * sob + n * son, out_dtype, acc);
+  }
+}
+
+template <typename T>
+__global__ void pack_rows_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
+                                 T* __restrict__ out, int N, int D, int Dp, int64_t total) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % Dp);
+    const int64_t rn = i / Dp;
+    const int64_t n = rn % N;
+    const int64_t b = rn / N;
+    out[i] = d < D ? x[b * sxb + n * sxn + d * sxd] : Elem<T>::from_f(0.0f);
+  }
+}
+
+template <typename T>
+static int row_sqnorm_typed(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                            const int64_t* xs, void* out, int out_dtype, const int64_t* os,
+                            cudaStream_t s) {
+  const int64_t rows = B * N;
+  const int threads = 256;
+  int64_t blocks = (rows + 7) / 8;
+  const int sms = sm_count_current();
+  const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 16 : 2048;
+  if (blocks > cap) blocks = cap;
+  if (out_dtype == dtype)
+    row_sqnorm_kernel<T, true><<<static_cast<int>(blocks), threads, 0, s>>>(
+        static_cast<const T*>(x), xs[0], xs[1], xs[2], out, out_dtype, os[0], os[1],
+        static_cast<int>(N), static_cast<int>(D), rows);
+  else
+    row_sqnorm_kernel<T, false><<<static_cast<int>(blocks), threads, 0, s>>>(
+        static_cast<const T*>(x), xs[0], xs[1], xs[2], out, out_dtype, os[0], os[1],
+        static_cast<int>(N), static_cast<int>(D), rows);
+  return check_launch("row_sqnorm_kernel");
+}
+
+template <typename T>
+static int pack_rows_typed(const void* x, int64_t B, int64_t N, int64_t D, const int64_t* xs,
+                           void* out, int64_t Dp, cudaStream_t s) {
+  const int64_t total = B * N * Dp;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  const int sms = sm_count_current();
+  const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 32 : 4096;
+  if (blocks > cap) blocks = cap;
+  pack_rows_kernel<T><<<static_cast<int>(blocks), threads, 0, s>>>(
+      static_cast<const T*>(x), xs[0], xs[1], xs[2], static_cast<T*>(out), static_cast<int>(N),
+      static_cast<int>(D), static_cast<int>(Dp), total);
+  return check_launch("pack_rows_kernel");
+}
+
+}  // namespace fk
+
+using namespace fk;
+
+extern "C" int fk_row_sqnorm(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                             const int64_t* x_strides3, void* out, int out_dtype,
+                             const int64_t* out_strides2, void* stream) {
+  if (B < 0 || N < 0 || D <= 0) return fail(FK_ERR_INVALID_ARG, "fk_row_sqnorm: bad sizes");
+  if (B == 0 || N == 0) return FK_OK;
+  if (!x || !out || !x_strides3 || !out_strides2)
+    return fail(FK_ERR_INVALID_ARG, "fk_row_sqnorm: null pointer argument");
+  if (out_dtype != dtype && out_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_row_sqnorm: out dtype must equal x dtype or be f32");
+  if (N >= (1ll << 31) || D >= (1ll << 31))
+    return fail(FK_ERR_UNSUPPORTED, "fk_row_sqnorm: sizes exceed 32-bit");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case FK_F16:
+      return row_sqnorm_typed<__half>(x, dtype, B, N, D, x_strides3, out, out_dtype, out_strides2, s);
+    case FK_BF16:
+      return row_sqnorm_typed<__nv_bfloat16>(x, dtype, B, N, D, x_strides3, out, out_dtype,
+                                             out_strides2, s);
+    case FK_F32:
+      return row_sqnorm_typed<float>(x, dtype, B, N, D, x_strides3, out, out_dtype, out_strides2, s);
+    default:
+      return fail(FK_ERR_INVALID_ARG, "fk_row_sqnorm: unsupported dtype %d", dtype);
+  }
+}
+
+extern "C" int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                            const int64_t* x_strides3, void* out, int64_t Dp, void* stream) {
+  if (B < 0 || N < 0 || D <= 0 || Dp < D) return fail(FK_ERR_INVALID_ARG, "fk_pack_rows: bad sizes");
+  if (B == 0 || N == 0) return FK_OK;
+  if (!x || !out || !x_strides3) return fail(FK_ERR_INVALID_ARG, "fk_pack_rows: null pointer");
+  if (N >= (1ll << 31) || Dp >= (1ll << 31))
+    return fail(FK_ERR_UNSUPPORTED, "fk_pack_rows: sizes exceed 32-bit");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case FK_F16: return pack_rows_typed<__half>(x, B, N, D, x_strides3, out, Dp, s);
+    case FK_BF16: return pack_rows_typed<__nv_bfloat16>(x, B, N, D, x_strides3, out, Dp, s);
+    case FK_F32: return pack_rows_typed<float>(x, B, N, D, x_strides3, out, Dp, s);
+    default: return fail(FK_ERR_INVALID_ARG, "fk_pack_rows: unsupported dtype %d", dtype);
+  }
+}

@@ -1,0 +1,381 @@
+"""Out-of-core / multi-GPU Lloyd k-means, drop-in for flash_kmeans.kmeans_large.
+
+Contract of the reference (kmeans_large.py:33-421): x (N, D) lives in host
+memory (ideally pinned) and is streamed to the GPUs in blocks of ``BLOCK_N``
+points; the blocks are partitioned contiguously over the devices
+(kmeans_large.py:69-80); every iteration each device assigns its blocks and
+accumulates per-cluster float32 sums and int32 counts, the partial sums are
+reduced across devices, and the centroids are finalized.  On a tolerance
+break the NEW centroids are returned (kmeans_large.py:251-258).  With one
+device the labels and centroids stay on that device; with several they are
+returned on the host (labels in pinned memory).
+
+B200 design:
+* per device a copy stream and a compute stream over two block buffers; the
+  copy of block i+1 (and of the next iteration's first blocks) overlaps the
+  assignment of block i, ordered by events only (no host waits);
+* x_sq per block is computed once and kept on the device;
+* the assignment kernel also produces the block's histogram, which the
+  accumulate step reuses (no separate histogram pass);
+* reduction: every device ends with identical sums/counts after an NCCL
+  all-reduce (single-process communicator over the devices, or the process
+  group when one process drives one GPU), then finalizes its own replica, so
+  no broadcast is needed.
+"""
+from __future__ import annotations
+
+import time
+import warnings
+from typing import Optional
+
+import torch
+
+from . import _native as nat
+from . import _ops
+
+
+def _resolve_devices(device):
+    """device=None -> all visible GPUs; otherwise exactly that one device
+    (kmeans_large.py:18-30)."""
+    if device is None:
+        G = torch.cuda.device_count()
+        if G == 0:
+            raise RuntimeError("No CUDA devices available")
+        return [torch.device(f"cuda:{i}") for i in range(G)]
+    return [torch.device(device)]
+
+
+def partition_blocks(N: int, BLOCK_N: int, G: int):
+    """Contiguous block partition of N points over G devices
+    (kmeans_large.py:69-80).  Returns (blocks_per_gpu, point_start, point_end)."""
+    num_blocks = (N + BLOCK_N - 1) // BLOCK_N
+    blocks_per_gpu = [(num_blocks // G) + (1 if g < (num_blocks % G) else 0) for g in range(G)]
+    block_start = [0] * G
+    for g in range(1, G):
+        block_start[g] = block_start[g - 1] + blocks_per_gpu[g - 1]
+    point_start = [block_start[g] * BLOCK_N for g in range(G)]
+    point_end = [min(point_start[g] + blocks_per_gpu[g] * BLOCK_N, N) for g in range(G)]
+    return blocks_per_gpu, point_start, point_end
+
+
+class _DeviceLane:
+    """Per-device streaming pipeline for one contiguous slice of x."""
+
+    def __init__(self, dev, x_host, p0, p1, BLOCK_N, K, D, dtype):
+        self.dev = dev
+        self.x_host = x_host
+        self.p0, self.p1 = p0, p1
+        self.BLOCK_N = BLOCK_N
+        self.blocks = [(n0, min(n0 + BLOCK_N, p1)) for n0 in range(p0, p1, BLOCK_N)]
+        self.K, self.D, self.dtype = K, D, dtype
+        with torch.cuda.device(dev):
+            self.copy_stream = torch.cuda.Stream(device=dev)
+            self.compute_stream = torch.cuda.Stream(device=dev)
+            nb = min(BLOCK_N, p1 - p0)
+            self.xbuf = [_ops.empty_rows(1, nb, D, dtype, dev) for _ in range(2)]
+            self.stage = None
+            if x_host.dtype != dtype or not (x_host.is_contiguous() and self.xbuf[0].is_contiguous()):
+                self.stage = [torch.empty((nb, D), dtype=x_host.dtype, device=dev) for _ in range(2)]
+            self.loaded = [torch.cuda.Event() for _ in range(2)]
+            self.free = [torch.cuda.Event() for _ in range(2)]
+            self.labels = torch.empty((1, p1 - p0), dtype=torch.int32, device=dev)
+            self.xsq = [None] * len(self.blocks)
+            self.c_cur = _ops.empty_rows(1, K, D, dtype, dev)
+            self.c_nxt = _ops.empty_rows(1, K, D, dtype, dev)
+            self.csq = torch.empty((1, K), dtype=torch.float32, device=dev)
+            self.sums = torch.empty((1, K, D), dtype=torch.float32, device=dev)
+            self.cnt = torch.empty((1, K), dtype=torch.int32, device=dev)
+            self.hist = torch.empty((1, K), dtype=torch.int32, device=dev)
+            self.stat = torch.zeros(4, dtype=torch.int32, device=dev)
+            self.csq_valid = False
+            lib = nat.load()
+            self.ws_a = torch.empty(lib.fk_assign_workspace_size(1, K, nat.dtype_code(dtype)),
+                                    dtype=torch.uint8, device=dev)
+            self.ws_u = torch.empty(lib.fk_centroid_accumulate_workspace_size(1, nb, K),
+                                    dtype=torch.uint8, device=dev)
+        # Copies form one sequence over passes: element s streams block s % nb
+        # into buffer slot s % 2, so consecutive copies always alternate slots.
+        self._issued = 0
+        self._ahead = []   # (block, slot) copied or in flight, not yet computed
+        self._pass = 0
+
+    # ---------------------------------------------------------------- loads
+    def _issue_load(self, blk: int, slot: int) -> None:
+        n0, n1 = self.blocks[blk]
+        nb = n1 - n0
+        cs = self.copy_stream
+        with torch.cuda.device(self.dev), torch.cuda.stream(cs):
+            cs.wait_event(self.free[slot])
+            dst = self.xbuf[slot][0, :nb]
+            src = self.x_host[n0:n1]
+            if self.stage is None:
+                dst.copy_(src, non_blocking=True)
+            else:
+                st = self.stage[slot][:nb]
+                st.copy_(src, non_blocking=True)
+                dst.copy_(st)
+            self.loaded[slot].record(cs)
+
+    def _prefetch_one(self) -> None:
+        nblk = len(self.blocks)
+        blk, slot = self._issued % nblk, self._issued % 2
+        self._issue_load(blk, slot)
+        self._ahead.append((blk, slot))
+        self._issued += 1
+
+    def _refill(self, wrap: bool) -> None:
+        """Keep two copies in flight; cross into the next pass only if `wrap`."""
+        nblk = len(self.blocks)
+        limit = (self._pass + (2 if wrap else 1)) * nblk
+        while len(self._ahead) < 2 and self._issued < limit:
+            self._prefetch_one()
+
+    # -------------------------------------------------------------- compute
+    def run_pass(self, assign_only: bool = False, wrap: bool = False) -> None:
+        """Assign (and accumulate) every block of this lane once.  With `wrap`
+        the first copies of the next pass are queued as buffers free up."""
+        lib = nat.load()
+        ks = self.compute_stream
+        K, D = self.K, self.D
+        with torch.cuda.device(self.dev), torch.cuda.stream(ks):
+            if not assign_only:
+                self.sums.zero_()
+                self.cnt.zero_()
+            s = nat.stream_handle(self.dev)
+            status = nat.ptr(self.stat[1:2])
+            self._refill(wrap)
+            for i, (n0, n1) in enumerate(self.blocks):
+                blk, slot = self._ahead.pop(0)
+                assert blk == i, (blk, i)
+                nb = n1 - n0
+                ks.wait_event(self.loaded[slot])
+                xb = self.xbuf[slot][:, :nb]
+                if self.xsq[i] is None:
+                    self.xsq[i] = _ops.row_sqnorm(xb)
+                xsq = self.xsq[i]
+                lo, hi = n0 - self.p0, n1 - self.p0
+                out = self.labels[:, lo:hi]
+                c_sq = self.csq if self.csq_valid else None
+                if not assign_only:
+                    self.hist.zero_()
+                nat.check(lib.fk_assign(
+                    nat.ptr(xb), nat.ptr(self.c_cur), nat.ptr(xsq), nat.ptr(c_sq), nat.ptr(out),
+                    None if assign_only else nat.ptr(self.hist), nat.dtype_code(xb.dtype),
+                    nat.dtype_code(xsq.dtype), nat.FK_F32, 1, nb, K, D, nat.strides(xb, 3),
+                    nat.strides(self.c_cur, 3), nat.strides(xsq, 2), nat.strides(self.csq, 2),
+                    nat.strides(out, 2), nat.ptr(self.ws_a), self.ws_a.numel(), status, s),
+                    "fk_assign")
+                if not assign_only:
+                    nat.check(lib.fk_centroid_accumulate(
+                        nat.ptr(xb), nat.dtype_code(xb.dtype), 1, nb, K, D, nat.strides(xb, 3),
+                        nat.ptr(out), nat.FK_I32, nat.strides(out, 2), nat.ptr(self.hist),
+                        nat.ptr(self.sums), nat.ptr(self.cnt), nat.ptr(self.ws_u),
+                        self.ws_u.numel(), status, s), "fk_centroid_accumulate")
+                self.free[slot].record(ks)
+                self._refill(wrap)
+            self._pass += 1
+
+    def finalize(self) -> None:
+        lib = nat.load()
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.compute_stream):
+            nat.check(lib.fk_centroid_finalize(
+                nat.ptr(self.sums), nat.ptr(self.cnt), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
+                nat.dtype_code(self.dtype), 1, self.K, self.D, nat.strides(self.c_cur, 3),
+                nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 0,
+                nat.stream_handle(self.dev)), "fk_centroid_finalize")
+            self.csq_valid = True
+
+    def advance(self) -> None:
+        self.c_cur, self.c_nxt = self.c_nxt, self.c_cur
+
+    def read_stat(self):
+        host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+        with torch.cuda.device(self.dev):
+            host.copy_(self.stat, non_blocking=True)
+            self.compute_stream.synchronize()
+        return host[0:1].view(torch.float32).item(), int(host[1].item())
+
+
+def reduce_partials(sums: torch.Tensor, counts: torch.Tensor, process_group) -> None:
+    """In-place all-reduce (sum) of one process's partial sums and counts.
+
+    This is the iteration's only exchange: K*D float32 sums plus K int32
+    counts.  Works with any torch.distributed backend (NCCL on GPUs, gloo for
+    host tensors)."""
+    import torch.distributed as dist
+    dist.all_reduce(sums, group=process_group)
+    dist.all_reduce(counts, group=process_group)
+
+
+def broadcast_centroids(c0: torch.Tensor, process_group) -> torch.Tensor:
+    """Make every process start from group rank 0's initial centroids."""
+    import torch.distributed as dist
+    src = dist.get_global_rank(process_group, 0) if process_group is not None else 0
+    dist.broadcast(c0, src=src, group=process_group)
+    return c0
+
+
+def _allreduce(lanes, process_group=None) -> None:
+    """Sum sums/counts over all lanes so every lane holds the total."""
+    if process_group is not None:
+        ln = lanes[0]
+        with torch.cuda.device(ln.dev), torch.cuda.stream(ln.compute_stream):
+            reduce_partials(ln.sums, ln.cnt, process_group)
+        return
+    if len(lanes) == 1:
+        return
+    import torch.cuda.nccl as nccl
+    streams = [ln.compute_stream for ln in lanes]
+    nccl.all_reduce([ln.sums for ln in lanes], streams=streams)
+    nccl.all_reduce([ln.cnt for ln in lanes], streams=streams)
+
+
+def _check_status(code: int) -> None:
+    if code:
+        raise RuntimeError(f"flash_kmeans device error {code}: {nat.device_status_message(code)}")
+
+
+def kmeans_largeN(
+    x: torch.Tensor,
+    n_clusters: int,
+    max_iters: int = 100,
+    tol: float = 0.0,
+    verbose: bool = False,
+    BLOCK_N=1048576,
+    init_centroids: Optional[torch.Tensor] = None,
+    device: Optional[torch.device] = None,
+    dtype: Optional[torch.dtype] = None,
+    *,
+    process_group=None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Lloyd k-means for x (N, D) in host memory, streamed in blocks of BLOCK_N.
+
+    ``device=None`` uses every visible GPU (one host thread drives them);
+    a device pins the run to that GPU.  ``process_group`` (extension): x is
+    this process's contiguous shard, the process drives one GPU (``device``
+    or the current one) and partial sums are all-reduced over the group;
+    labels of the shard are returned on the device.
+
+    Returns (cluster_ids int32 (N,), centroids (K, D)).
+    """
+    if not torch.cuda.is_available():
+        raise RuntimeError("kmeans_largeN needs CUDA (this build has no CPU fallback)")
+    if max_iters < 1:
+        raise ValueError("max_iters must be >= 1")
+    distributed = process_group is not None
+    if distributed:
+        devices = [torch.device(device) if device is not None
+                   else torch.device("cuda", torch.cuda.current_device())]
+    else:
+        devices = _resolve_devices(device)
+    G = len(devices)
+    dtype = dtype or x.dtype
+
+    if not x.is_pinned() and G > 1:
+        warnings.warn(
+            "x is not in pinned memory. H2D transfers will not overlap with compute. "
+            "Use x = x.pin_memory() for best multi-GPU performance.",
+            stacklevel=2,
+        )
+
+    N, D = x.shape
+    K = int(n_clusters)
+    blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
+    active = [g for g in range(G) if blocks_per_gpu[g] > 0]
+    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype)
+             for g in active]
+    primary = lanes[0]
+
+    # ---- initial centroids (replicated)
+    if init_centroids is not None:
+        c0 = init_centroids.reshape(K, D)
+    elif distributed:
+        # x is this process's shard: sample on every rank, keep rank 0's
+        c0 = x[torch.randint(0, N, (K,), device="cpu", dtype=torch.int32)]
+        c0 = broadcast_centroids(c0.to(primary.dev, dtype=dtype).contiguous(), process_group)
+    else:
+        c0 = x[torch.randint(0, N, (K,), device="cpu", dtype=torch.int32)]
+    for ln in lanes:
+        with torch.cuda.device(ln.dev), torch.cuda.stream(ln.compute_stream):
+            ln.c_cur[0].copy_(c0.to(ln.dev, dtype=dtype, non_blocking=True))
+            ln.stat.zero_()
+
+    need_sync = tol > 0 or verbose
+    tol_r = float(torch.tensor(float(tol), dtype=dtype))
+    for it in range(max_iters):
+        t0 = time.time()
+        # with wrap, the next pass's first copies are queued during this pass
+        # and overlap the reduction below
+        for ln in lanes:
+            ln.run_pass(wrap=it + 1 < max_iters)
+        _allreduce(lanes, process_group)
+        for ln in lanes:
+            ln.finalize()
+        if need_sync:
+            shift, code = primary.read_stat()
+            _check_status(code)
+            if verbose:
+                print(f"Iter {it}, center shift: {shift:.6f}, time: {time.time() - t0:.2f}s")
+            if shift < tol_r:
+                for ln in lanes:
+                    ln.advance()
+                break
+        for ln in lanes:
+            ln.advance()
+
+    # drain any prefetched copies before buffers can be reused or freed
+    for ln in lanes:
+        with torch.cuda.device(ln.dev):
+            ln.copy_stream.synchronize()
+            ln.compute_stream.synchronize()
+        _, code = ln.read_stat()
+        _check_status(code)
+
+    centroids = primary.c_cur[0]
+    centroids = centroids if centroids.is_contiguous() else centroids.contiguous()
+    if G == 1 or distributed:
+        return primary.labels[0], centroids
+    labels = torch.empty((N,), dtype=torch.int32, pin_memory=True)
+    for ln in lanes:
+        labels[ln.p0:ln.p1].copy_(ln.labels[0])
+    return labels, centroids.cpu()
+
+
+def kmeans_largeN_assign(
+    x: torch.Tensor,
+    centroids: torch.Tensor,
+    BLOCK_N=1048576,
+    device: Optional[torch.device] = None,
+    dtype: Optional[torch.dtype] = None,
+) -> torch.Tensor:
+    """Labels for x (N, D) in host memory against centroids (K, D)
+    (kmeans_large.py:288-421).  One device -> labels on it; several -> pinned host."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("kmeans_largeN_assign needs CUDA (this build has no CPU fallback)")
+    devices = _resolve_devices(device)
+    G = len(devices)
+    dtype = dtype or x.dtype
+    N, D = x.shape
+    assert centroids.shape[1] == D, "centroids and x must have the same feature dimension"
+    K = centroids.shape[0]
+    blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
+    active = [g for g in range(G) if blocks_per_gpu[g] > 0]
+    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype)
+             for g in active]
+    for ln in lanes:
+        with torch.cuda.device(ln.dev), torch.cuda.stream(ln.compute_stream):
+            ln.c_cur[0].copy_(centroids.to(ln.dev, dtype=dtype, non_blocking=True))
+            ln.stat.zero_()
+    for ln in lanes:
+        ln.run_pass(assign_only=True)
+    for ln in lanes:
+        with torch.cuda.device(ln.dev):
+            ln.compute_stream.synchronize()
+        _, code = ln.read_stat()
+        _check_status(code)
+    if G == 1:
+        return lanes[0].labels[0]
+    labels = torch.empty((N,), dtype=torch.int32, pin_memory=True)
+    for ln in lanes:
+        labels[ln.p0:ln.p1].copy_(ln.labels[0])
+    return labels

@@ -1,0 +1,189 @@
+"""Batched Lloyd k-means driver, drop-in for flash_kmeans.kmeans_triton_impl.
+
+``batch_kmeans_Euclid`` keeps the reference's contract
+(kmeans_triton_impl.py:55-115): random-point init with replacement from the
+CUDA RNG when no centroids are given, x_sq precomputed once in x's dtype, one
+assignment + update + shift per iteration, ``break`` when the shift drops
+below ``tol`` (returning the centroids that produced the last labels), and the
+result ``(cluster_ids int32 (B,N), centroids (B,K,D) x.dtype, n_iters)``.
+
+Per iteration the B200 build launches: fk_assign (labels + fused histogram),
+fk_centroid_accumulate (scan, scatter, segmented sums) and fk_centroid_finalize
+(means, next ||c||^2, shift, and zeroing of the accumulators for the next
+iteration) -- six kernels, no memsets.  The host reads the 8-byte
+(shift, status) record only when ``tol > 0`` or ``verbose`` needs it; with
+``tol <= 0`` the shift can never be below tol, so iterations are queued back
+to back with no host synchronisation.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from . import _ops
+
+
+def _round_tol(tol: float, dtype: torch.dtype) -> float:
+    # `center_shift < tol` on a 0-dim tensor of x.dtype compares in that dtype
+    return float(torch.tensor(float(tol), dtype=dtype))
+
+
+class LloydEngine:
+    """Buffers and launches for batched Lloyd iterations on one device.
+
+    Reusable across fits of the same shape: ``load(x, centroids)`` then
+    ``step()`` per iteration.  ``ids`` always holds the last labels and
+    ``centroids`` the centroids that produced them.
+    """
+
+    def __init__(self, B: int, N: int, K: int, D: int, dtype: torch.dtype, device):
+        self.B, self.N, self.K, self.D, self.dtype = B, N, K, D, dtype
+        self.device = torch.device(device)
+        dev = self.device
+        self.c_cur = _ops.empty_rows(B, K, D, dtype, dev)
+        self.c_nxt = _ops.empty_rows(B, K, D, dtype, dev)
+        self.ids = torch.empty((B, N), dtype=torch.int32, device=dev)
+        self.sums = torch.empty((B, K, D), dtype=torch.float32, device=dev)
+        self.hist = torch.empty((B, K), dtype=torch.int32, device=dev)
+        self.csq = torch.empty((B, K), dtype=torch.float32, device=dev)
+        # [0] shift (float32 bits), [1] device status, [2..3] spare
+        self.stat = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.stat_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        self.csq_valid = False
+        lib = nat.load()
+        self.ws_a = torch.empty(lib.fk_assign_workspace_size(B, K, nat.dtype_code(dtype)),
+                                dtype=torch.uint8, device=dev)
+        self.ws_u = torch.empty(lib.fk_centroid_accumulate_workspace_size(B, N, K),
+                                dtype=torch.uint8, device=dev)
+        self.x = None
+        self.x_sq = None
+
+    # ---------------------------------------------------------------- set-up
+    def load(self, x: torch.Tensor, centroids: torch.Tensor, x_sq: torch.Tensor | None = None):
+        self.x = _ops.ensure_tma(x)
+        self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
+        self.c_cur.copy_(centroids.view(self.B, self.K, self.D))
+        self.csq_valid = False
+        self.stat.zero_()
+        self.hist.zero_()
+        self.sums.zero_()
+
+    # ------------------------------------------------------------- iteration
+    def step(self, ev_assign=None) -> None:
+        """One Lloyd iteration: ids <- assign(centroids); c_nxt <- update; shift.
+
+        ``ev_assign``: optional (start, end) CUDA events recorded around the
+        assignment on the current stream (used by the benchmark)."""
+        lib = nat.load()
+        B, N, K, D = self.B, self.N, self.K, self.D
+        x, dev = self.x, self.device
+        s = nat.stream_handle(dev)
+        status = nat.ptr(self.stat[1:2])
+        c_sq = self.csq if self.csq_valid else None
+        if ev_assign is not None:
+            ev_assign[0].record()
+        nat.check(lib.fk_assign(
+            nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.x_sq), nat.ptr(c_sq), nat.ptr(self.ids),
+            nat.ptr(self.hist), nat.dtype_code(x.dtype), nat.dtype_code(self.x_sq.dtype),
+            nat.FK_F32, B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
+            nat.strides(self.x_sq, 2), nat.strides(self.csq, 2), nat.strides(self.ids, 2),
+            nat.ptr(self.ws_a), self.ws_a.numel(), status, s), "fk_assign")
+        if ev_assign is not None:
+            ev_assign[1].record()
+        nat.check(lib.fk_centroid_accumulate(
+            nat.ptr(x), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.ptr(self.ids),
+            nat.FK_I32, nat.strides(self.ids, 2), nat.ptr(self.hist), nat.ptr(self.sums),
+            nat.ptr(self.hist), nat.ptr(self.ws_u), self.ws_u.numel(), status, s),
+            "fk_centroid_accumulate")
+        nat.check(lib.fk_centroid_finalize(
+            nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
+            nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
+            nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 1, s),
+            "fk_centroid_finalize")
+        self.csq_valid = True
+
+    def advance(self) -> None:
+        """Adopt the updated centroids for the next iteration."""
+        self.c_cur, self.c_nxt = self.c_nxt, self.c_cur
+
+    def read_stat(self):
+        """(shift, device status) of the last step; synchronises the stream."""
+        self.stat_host.copy_(self.stat, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        shift = self.stat_host[0:1].view(torch.float32).item()
+        code = int(self.stat_host[1].item())
+        return shift, code
+
+    def raise_on_status(self, code: int) -> None:
+        if code:
+            raise RuntimeError(f"flash_kmeans device error {code}: {nat.device_status_message(code)}")
+
+    def result_centroids(self) -> torch.Tensor:
+        c = self.c_cur
+        return c if c.is_contiguous() else c.contiguous()
+
+
+def batch_kmeans_Euclid(
+    x,
+    n_clusters,
+    max_iters=100,
+    tol=0.0,
+    init_centroids=None,
+    verbose=False,
+    *,
+    use_heuristic=True,
+):
+    """Batched k-means (Euclidean) on CUDA; reference kmeans_triton_impl.py:55-115.
+
+    Args:
+        x: (B, N, D) float16 / bfloat16 / float32 CUDA tensor.
+        n_clusters: K.
+        max_iters: maximum number of Lloyd iterations (>= 1).
+        tol: stop when the max centroid shift is below tol.
+        init_centroids: optional (B, K, D) initial centroids.
+        verbose: print the shift per iteration.
+        use_heuristic: accepted for compatibility, ignored.
+    Returns:
+        cluster_ids (B, N) int32, centroids (B, K, D) x.dtype, number of iterations.
+    """
+    if not torch.cuda.is_available() or not x.is_cuda:
+        raise RuntimeError("batch_kmeans_Euclid needs a CUDA tensor (this build has no CPU fallback)")
+    if max_iters < 1:
+        raise ValueError("max_iters must be >= 1")
+    B, N, D = x.shape
+    K = int(n_clusters)
+    if init_centroids is None:
+        indices = torch.randint(0, N, (B, K), device=x.device)
+        centroids = torch.gather(x, dim=1, index=indices[..., None].expand(-1, -1, D))
+    else:
+        centroids = init_centroids
+    centroids = centroids.view(B, K, D)
+
+    with torch.cuda.device(x.device):
+        eng = LloydEngine(B, N, K, D, x.dtype, x.device)
+        eng.load(x, centroids)
+        need_sync = tol > 0 or verbose
+        tol_r = _round_tol(tol, x.dtype)
+        it = 0
+        for it in range(max_iters):
+            eng.step()
+            if need_sync:
+                shift, code = eng.read_stat()
+                eng.raise_on_status(code)
+                if verbose:
+                    print(f"Iter {it}, center shift: {shift:.6f}")
+                if shift < tol_r:
+                    break
+            eng.advance()
+        if not need_sync:
+            _, code = eng.read_stat()
+            eng.raise_on_status(code)
+        return eng.ids, eng.result_centroids(), it + 1
+
+
+def batch_kmeans_Cosine(x, n_clusters, max_iters=100, tol=0.0, init_centroids=None, verbose=False):
+    raise NotImplementedError("cosine k-means is not part of the B200 Euclidean build")
+
+
+def batch_kmeans_Dot(x, n_clusters, max_iters=100, tol=0.0, init_centroids=None, verbose=False):
+    raise NotImplementedError("dot-product k-means is not part of the B200 Euclidean build")

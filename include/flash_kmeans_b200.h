@@ -1,0 +1,135 @@
+/*
+ * flash_kmeans_b200.h -- C ABI of the B200 (sm_100a) Lloyd-iteration kernels.
+ *
+ * This is the drop-in boundary under the Python package `flash_kmeans`
+ * (flash-kmeans_b200/flash_kmeans/).  Every entry point takes plain device
+ * pointers, element strides and sizes, launches on the caller's CUDA stream
+ * (`stream` is a cudaStream_t; NULL means the legacy default stream) and never
+ * synchronises.  Buffers are caller-owned; scratch memory is the caller's
+ * `workspace` (size from the matching *_workspace_size query).  Nothing is
+ * allocated and no global mutable state is kept apart from one-time lookups
+ * (driver entry point, per-device SM count, kernel attributes), so one host
+ * thread may drive several devices by switching the current device.
+ *
+ * Errors: functions return FK_OK (0) or an fk_status code; fk_last_error()
+ * returns a thread-local message for the last failure.  Kernels that can
+ * detect bad data or a stalled pipeline report it asynchronously through the
+ * optional `dev_status` word (an int32 in device memory, zero on entry):
+ * the caller reads it back at its next synchronisation point.
+ *
+ * Reference interfaces replaced (paths inside svg-project/flash-kmeans):
+ *   fk_row_sqnorm          <- x_sq precompute, flash_kmeans/kmeans_triton_impl.py:84-87
+ *                             and flash_kmeans/interface.py:240-245
+ *   fk_assign              <- euclid_assign_triton, flash_kmeans/assign_euclid_triton.py:1238-1412
+ *                             (kernels _euclid_assign_kernel :804-917 and
+ *                             _euclid_assign_kernel_split_d :933-1030)
+ *   fk_centroid_accumulate <- triton_centroid_update_sorted_euclid accumulate phase,
+ *                             flash_kmeans/centroid_update_triton.py:316-376
+ *                             (kernel _centroid_update_chunk_kernel :188-263)
+ *   fk_centroid_finalize   <- the same function's finalize, centroid_update_triton.py:378-386,
+ *                             plus the shift of kmeans_triton_impl.py:16 and the
+ *                             c_sq of assign_euclid_triton.py:1282-1283
+ *   fk_pack_rows           <- no reference counterpart: repacks rows whose
+ *                             stride is not a multiple of 16 bytes for TMA
+ */
+#ifndef FLASH_KMEANS_B200_H
+#define FLASH_KMEANS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FK_ABI_VERSION 1
+
+/* element types */
+enum fk_dtype { FK_F16 = 0, FK_BF16 = 1, FK_F32 = 2, FK_I32 = 3, FK_I64 = 4 };
+
+/* host-side status codes */
+enum fk_status {
+  FK_OK = 0,
+  FK_ERR_INVALID_ARG = 1, /* null pointer, negative size, bad stride, dtype mismatch */
+  FK_ERR_UNSUPPORTED = 2, /* layout/size the kernels do not take (e.g. rows not 16-byte aligned) */
+  FK_ERR_WORKSPACE = 3,   /* workspace missing, too small or misaligned */
+  FK_ERR_CUDA = 4,        /* a CUDA runtime call or kernel launch failed */
+  FK_ERR_TMA = 5          /* tensor-map encoding failed */
+};
+
+/* device-side codes written to *dev_status (first error wins) */
+enum fk_device_status {
+  FK_DEV_OK = 0,
+  FK_DEV_BAD_LABEL = 101,      /* a cluster id outside [0, K) was fed to the update */
+  FK_DEV_WAIT_TIMEOUT = 102    /* a pipeline wait in the assign kernel exceeded its limit */
+};
+
+int fk_abi_version(void);
+const char* fk_status_string(int status);
+const char* fk_last_error(void);
+/* SM count of the current device (cached); <0 on error. */
+int fk_device_sm_count(void);
+
+/* 1 if (ptr, strides) can be read by the TMA-based assignment directly:
+ * unit innermost stride, 16-byte aligned base, 16-byte multiple outer strides. */
+int fk_tma_compatible(const void* ptr, int dtype, int64_t D, const int64_t* strides3);
+
+/* Row squared norms out[b,n] = sum_d x[b,n,d]^2.
+ * out_dtype == dtype: rounded like `(x ** 2).sum(-1)` evaluated in that dtype
+ * (per-element square rounded, float32 accumulation, one final rounding);
+ * out_dtype == FK_F32: computed entirely in float32. */
+int fk_row_sqnorm(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                  const int64_t* x_strides3, void* out, int out_dtype,
+                  const int64_t* out_strides2, void* stream);
+
+/* Copy x (B,N,D, any strides) into a contiguous (B,N,Dp) buffer, Dp >= D, with
+ * zeros in columns [D, Dp).  Used to make rows TMA-addressable. */
+int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                 const int64_t* x_strides3, void* out, int64_t Dp, void* stream);
+
+/* Nearest centroid by squared Euclidean distance.
+ *   x (B,N,D), centroids (B,K,D): dtype FK_F16 / FK_BF16 / FK_F32, TMA-compatible.
+ *   x_sq (B,N): xsq_dtype; c_sq (B,K) optional (NULL -> computed from centroids).
+ *   out (B,N) int32.  counts (B,K) int32 optional: if given, out's histogram is
+ *   ADDED to it (the update's histogram, fused).
+ * Distance rounding follows the reference's torch path: with x_sq in x's
+ * 16-bit dtype the chain is round(round(x_sq - 2*round(x.c)) + c_sq) in that
+ * dtype; otherwise float32 (for float32 x the dot products are 3xTF32 on the
+ * tensor cores).  Ties resolve to the lowest centroid index.
+ * Requires K <= 1<<20, N < 2^31. */
+size_t fk_assign_workspace_size(int64_t B, int64_t K, int dtype);
+int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
+              int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,
+              int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
+              const int64_t* c_strides3, const int64_t* xsq_strides2,
+              const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
+              size_t workspace_bytes, int32_t* dev_status, void* stream);
+
+/* Per-cluster float32 sums (B,K,D contiguous) and int32 counts (B,K contiguous)
+ * of the rows of x grouped by ids (B,N; FK_I32 or FK_I64), ADDED to `sums`
+ * and `counts`.  `hist` (B,K) optional: the histogram of exactly these ids
+ * (e.g. produced by fk_assign's `counts`); NULL -> computed here.
+ * Grouping is a counting sort (histogram, scan, scatter) followed by a
+ * segmented sum over the sorted order. */
+size_t fk_centroid_accumulate_workspace_size(int64_t B, int64_t N, int64_t K);
+int fk_centroid_accumulate(const void* x, int dtype, int64_t B, int64_t N, int64_t K, int64_t D,
+                           const int64_t* x_strides3, const void* ids, int ids_dtype,
+                           const int64_t* ids_strides2, const int32_t* hist, float* sums,
+                           int32_t* counts, void* workspace, size_t workspace_bytes,
+                           int32_t* dev_status, void* stream);
+
+/* new = counts ? sums / counts : old, cast to dtype (reference finalize).
+ * Optional outputs: csq_out (B,K) float32 = (new ** 2).sum(-1) rounded in dtype;
+ * shift_out (one float32) = max_k ||new_k - old_k|| rounded in dtype.
+ * reset_accumulators != 0: sums and counts are set to zero after being read,
+ * ready for the next iteration's accumulation.
+ * `new_centroids` may not alias `old_centroids`. */
+int fk_centroid_finalize(float* sums, int32_t* counts, const void* old_centroids,
+                         void* new_centroids, int dtype, int64_t B, int64_t K, int64_t D,
+                         const int64_t* old_strides3, const int64_t* new_strides3,
+                         float* csq_out, float* shift_out, int reset_accumulators, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASH_KMEANS_B200_H */

@@ -1,0 +1,71 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol.
+
+No compute call is made here (this runs on CPU-only machines); only pure host
+entry points (version, status strings, the TMA layout predicate, workspace
+sizes) are exercised.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "flash_kmeans_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(fk_[a-z0-9_]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from flash_kmeans import _native
+    return _native.load()
+
+
+def test_header_declares_the_api():
+    names = _declared()
+    for must in ("fk_assign", "fk_centroid_accumulate", "fk_centroid_finalize", "fk_row_sqnorm",
+                 "fk_pack_rows", "fk_abi_version"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    missing = [n for n in _declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    from flash_kmeans import _native
+    assert set(_native.SIGNATURES) == set(_declared())
+
+
+def test_host_only_entry_points(lib):
+    assert lib.fk_abi_version() == 1
+    assert lib.fk_status_string(0) == b"ok"
+    assert b"workspace" in lib.fk_status_string(3)
+    assert lib.fk_assign_workspace_size(32, 1000, 0) >= 32 * 1024 * 4
+    assert lib.fk_centroid_accumulate_workspace_size(32, 75600, 1000) >= 2 * 32 * 75600 * 4
+    st = (ctypes.c_int64 * 3)(75600 * 128, 128, 1)
+    assert lib.fk_tma_compatible(ctypes.c_void_p(1 << 20), 0, 128, st) == 1
+    st_bad = (ctypes.c_int64 * 3)(75600 * 100, 100, 1)  # 200-byte rows
+    assert lib.fk_tma_compatible(ctypes.c_void_p(1 << 20), 0, 100, st_bad) == 0
+    assert lib.fk_tma_compatible(ctypes.c_void_p((1 << 20) + 8), 0, 128, st) == 0
+
+
+def test_invalid_arguments_fail_on_host(lib):
+    """Argument validation happens before any CUDA call."""
+    from flash_kmeans import _native
+    st = (ctypes.c_int64 * 3)(1, 1, 1)
+    rc = lib.fk_assign(None, None, None, None, None, None, 0, 0, 0, 1, 1, 0, 1, st, st, st, st, st,
+                       None, 0, None, None)
+    assert rc == 1
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _native.check(rc, "fk_assign")
+    assert b"bad sizes" in lib.fk_last_error()
+    rc = lib.fk_centroid_accumulate(None, 0, 1, 1, 4, 8, st, None, 3, st, None, None, None, None,
+                                    0, None, None)
+    assert rc == 1

@@ -1,0 +1,192 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle and the golden vectors.
+
+Every computation here goes through the C ABI (flash_kmeans._ops -> ctypes ->
+libflashkmeans_b200.so); the oracle (numpy) is the checker only.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from _parity import assert_centroids, assert_labels, label_report
+from oracle import kmeans_oracle as ko
+
+pytestmark = pytest.mark.gpu
+
+TD = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+def _dev(a, dt):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to("cuda").to(TD[dt])
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def fk():
+    import flash_kmeans
+    from flash_kmeans import _native
+    _native.load()
+    return flash_kmeans
+
+
+# ----------------------------------------------------------------- row norms
+@pytest.mark.parametrize("dt", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("D", [1, 17, 128, 2048])
+def test_row_sqnorm_matches_oracle(fk, dt, D):
+    from flash_kmeans import _ops
+    rng = np.random.default_rng(D)
+    x = ko.round_to(rng.standard_normal((2, 301, D), dtype=np.float32), dt)
+    got = _np(_ops.row_sqnorm(_dev(x, dt)))
+    want = ko.row_sqnorm(x, dt)
+    # float32 accumulation order differs; the final rounding may differ by one ulp
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-6)
+    ulp = {"float16": 2 ** -10, "bfloat16": 2 ** -7, "float32": 1e-5}[dt]
+    assert rel.max() <= ulp * 1.01
+    assert (got != want).mean() < 0.02
+
+
+# ----------------------------------------------------------------- assignment
+@pytest.mark.parametrize("spec", cases.ASSIGN_CASES, ids=lambda s: s["name"])
+def test_assign_matches_golden_and_oracle(fk, spec):
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    x, c, xsq, xsq_dtype = cases.assign_inputs(spec)
+    dt = spec["dtype"]
+    ids = euclid_assign_triton(_dev(x, dt), _dev(c, dt), _dev(xsq, xsq_dtype))
+    torch.cuda.synchronize()
+    got = ids.cpu().numpy()
+    golden = np.load(cases.path(spec["name"]))["ids"]
+    assert_labels(x, c, got, golden, dt, spec["name"] + " vs reference")
+    want = ko.assign(x, c, xsq, dt, xsq_dtype=xsq_dtype)
+    assert_labels(x, c, got, want, dt, spec["name"] + " vs oracle")
+
+
+def test_assign_duplicate_centroids_take_lowest_index(fk):
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    spec = next(s for s in cases.ASSIGN_CASES if s.get("dup"))
+    x, c, xsq, xsq_dtype = cases.assign_inputs(spec)
+    ids = euclid_assign_triton(_dev(x, "float16"), _dev(c, "float16"), _dev(xsq, "float16"))
+    got = ids.cpu().numpy()
+    assert got.max() < spec["K"] // 2
+    np.testing.assert_array_equal(got, np.load(cases.path(spec["name"]))["ids"])
+
+
+SHAPES = [  # (B, N, K, D): tails in every dimension, both x-resident and split-D paths
+    (1, 1, 1, 16), (1, 5, 3, 8), (2, 127, 7, 64), (1, 129, 255, 128), (1, 300, 256, 32),
+    (1, 257, 257, 96), (3, 200, 19, 100), (1, 1000, 513, 17), (1, 640, 70, 192),
+    (1, 333, 300, 513), (1, 250, 64, 1000),
+]
+
+
+@pytest.mark.parametrize("dt", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_assign_shapes_vs_oracle(fk, dt, shape):
+    from flash_kmeans import _ops
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    B, N, K, D = shape
+    rng = np.random.default_rng(hash((dt,) + shape) % 2 ** 32)
+    x = ko.round_to(rng.standard_normal((B, N, D), dtype=np.float32), dt)
+    c = ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt)
+    xd = _dev(x, dt)
+    xsq = _ops.row_sqnorm(xd)
+    ids = euclid_assign_triton(xd, _dev(c, dt), xsq).cpu().numpy()
+    want = ko.assign(x, c, _np(xsq), dt)
+    assert_labels(x, c, ids, want, dt, f"{dt} {shape}")
+
+
+def test_assign_strided_inputs(fk):
+    """Non-contiguous x (transposed storage) and a sliced batch go through packing."""
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    rng = np.random.default_rng(5)
+    x = ko.round_to(rng.standard_normal((2, 64, 500), dtype=np.float32), "float16")
+    c = ko.round_to(rng.standard_normal((2, 40, 64), dtype=np.float32), "float16")
+    xt = _dev(x, "float16").transpose(1, 2)          # (2, 500, 64), stride_d = 500
+    xs = ko.round_to(np.swapaxes(x, 1, 2), "float16")
+    xsq = (xt.float() ** 2).sum(-1)
+    ids = euclid_assign_triton(xt, _dev(c, "float16"), xsq).cpu().numpy()
+    want = ko.assign(xs, c, _np(xsq), "float16", xsq_dtype="float32")
+    assert_labels(xs, c, ids, want, "float16", "strided")
+
+
+def test_assign_out_and_csq_arguments(fk):
+    from flash_kmeans import _ops
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    rng = np.random.default_rng(6)
+    x = ko.round_to(rng.standard_normal((2, 700, 64), dtype=np.float32), "float16")
+    c = ko.round_to(rng.standard_normal((2, 90, 64), dtype=np.float32), "float16")
+    xd, cd = _dev(x, "float16"), _dev(c, "float16")
+    xsq = _ops.row_sqnorm(xd)
+    out = torch.full((2, 700), -1, dtype=torch.int32, device="cuda")
+    csq = (cd.float() ** 2).sum(-1)
+    r = euclid_assign_triton(xd, cd, xsq, out=out, c_sq=csq)
+    assert r.data_ptr() == out.data_ptr()
+    base = euclid_assign_triton(xd, cd, xsq)
+    rep = label_report(x, c, out.cpu().numpy(), base.cpu().numpy(), "float16")
+    assert rep["bad"] == 0
+    with pytest.raises(ValueError):
+        euclid_assign_triton(xd, cd, xsq, num_warps=4)
+
+
+def test_assign_deterministic(fk):
+    from flash_kmeans import _ops
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(4, 20000, 128, device="cuda", generator=g).half()
+    c = torch.randn(4, 1000, 128, device="cuda", generator=g).half()
+    xsq = _ops.row_sqnorm(x)
+    a = euclid_assign_triton(x, c, xsq)
+    b = euclid_assign_triton(x, c, xsq)
+    assert torch.equal(a, b)
+
+
+# ------------------------------------------------------------------ update
+@pytest.mark.parametrize("spec", cases.UPDATE_CASES, ids=lambda s: s["name"])
+@pytest.mark.parametrize("idt", [torch.int32, torch.int64])
+def test_update_matches_golden(fk, spec, idt):
+    from flash_kmeans import triton_centroid_update_sorted_euclid
+    x, ids, old = cases.update_inputs(spec)
+    dt = spec["dtype"]
+    new = triton_centroid_update_sorted_euclid(_dev(x, dt), torch.from_numpy(ids).to("cuda", idt),
+                                               _dev(old, dt))
+    got = _np(new)
+    golden = np.load(cases.path(spec["name"]))["centroids"]
+    assert_centroids(got, golden, spec["name"])
+    # empty clusters are bit-identical to the old centroids
+    cnt = np.stack([np.bincount(ids[b], minlength=spec["K"]) for b in range(spec["B"])])
+    np.testing.assert_array_equal(got[cnt == 0], ko.round_to(old, dt)[cnt == 0])
+
+
+def test_update_accumulate_over_blocks(fk):
+    """Accumulating two halves equals the one-shot update (calculate_new=False path)."""
+    from flash_kmeans import triton_centroid_update_sorted_euclid as upd
+    rng = np.random.default_rng(9)
+    B, N, K, D = 1, 5000, 77, 128
+    x = _dev(rng.standard_normal((B, N, D), dtype=np.float32), "float32")
+    ids = torch.from_numpy(rng.integers(0, K, (B, N)).astype(np.int32)).cuda()
+    old = _dev(rng.standard_normal((B, K, D), dtype=np.float32), "float32")
+    sums = torch.zeros((B, K, D), device="cuda")
+    cnts = torch.zeros((B, K), dtype=torch.int32, device="cuda")
+    assert upd(x[:, :2000], ids[:, :2000], old, centroid_sums=sums, centroid_cnts=cnts,
+               calculate_new=False) is None
+    last = upd(x[:, 2000:], ids[:, 2000:], old, centroid_sums=sums, centroid_cnts=cnts,
+               calculate_new=True)
+    ref = ko.centroid_update(_np(x), ids.cpu().numpy(), _np(old), "float32")
+    assert_centroids(_np(last), ref, "accumulate")
+    np.testing.assert_array_equal(cnts.cpu().numpy()[0], np.bincount(ids.cpu().numpy()[0], minlength=K))
+
+
+def test_update_bad_label_reports_device_status(fk):
+    from flash_kmeans import _ops
+    from flash_kmeans._ops import DeviceStatus
+    x = torch.randn(1, 64, 32, device="cuda")
+    ids = torch.zeros(1, 64, dtype=torch.int32, device="cuda")
+    ids[0, 3] = 99  # K = 8
+    sums = torch.zeros(1, 8, 32, device="cuda")
+    cnt = torch.zeros(1, 8, dtype=torch.int32, device="cuda")
+    _ops.accumulate(x, ids, sums, cnt)
+    with pytest.raises(RuntimeError, match="outside"):
+        DeviceStatus.raise_if_set(x.device)
+    DeviceStatus.raise_if_set(x.device)  # cleared
+    assert int(cnt.sum()) == 63
