@@ -28,6 +28,8 @@
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
 // centroid chunk instead of staying resident.
+#include <type_traits>
+
 #include "fk_common.cuh"
 #include "fk_ptx.cuh"
 
@@ -111,6 +113,13 @@ struct Pack2<__half> {
   __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
     return __hlt2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   }
+  __device__ __forceinline__ static uint32_t ne_mask(uint32_t a, uint32_t b) {
+    return __hne2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  }
+  __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
+    const __half2 r = __hmin2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
   __device__ __forceinline__ static float lo(uint32_t v) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
   }
@@ -138,6 +147,15 @@ struct Pack2<__nv_bfloat16> {
     return __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
                        *reinterpret_cast<const __nv_bfloat162*>(&b));
   }
+  __device__ __forceinline__ static uint32_t ne_mask(uint32_t a, uint32_t b) {
+    return __hne2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+  }
+  __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
+    const __nv_bfloat162 r = __hmin2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
   __device__ __forceinline__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
   __device__ __forceinline__ static float hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
   __device__ __forceinline__ static uint32_t splat(float v) {
@@ -151,6 +169,112 @@ template <typename T>
 __device__ __forceinline__ float round16(float v) {
   return Elem<T>::round(v);
 }
+
+// Running argmin over a thread's row, split into kChains independent chains
+// (column pair p goes to chain p % kChains) so consecutive updates do not
+// wait on each other.  Columns are visited in increasing order within a
+// chain and updates need a strictly smaller value, so each chain keeps its
+// lowest-index minimum; result() merges the chains by (value, index).
+// A chain remembers the local position of its best column inside its
+// 32-column chunk plus the chunk id, which is refreshed once per chunk where
+// the best value changed (compared as values, so -0/+0 are one value).
+constexpr int kChains = 4;
+
+template <typename T>
+struct ArgminPacked {  // mode 0: two columns per 32-bit register
+  uint32_t best[kChains], loc[kChains], chunk[kChains];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      best[c] = Pack2<T>::kInf2;
+      loc[c] = 0;
+      chunk[c] = 0;
+    }
+  }
+  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint32_t* cw,
+                                          uint32_t xsq2, int col0) {
+    uint32_t prev[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) prev[c] = best[c];
+#pragma unroll
+    for (int pp = 0; pp < 16; ++pp) {
+      const int c = pp % kChains;
+      const uint32_t d =
+          Pack2<T>::dist(__uint_as_float(v[2 * pp]), __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
+      const uint32_t m = Pack2<T>::lt_mask(d, best[c]);
+      best[c] = Pack2<T>::min2(best[c], d);
+      loc[c] = ((static_cast<uint32_t>(pp) * 0x00010001u) & m) | (loc[c] & ~m);
+    }
+    const uint32_t cid2 = static_cast<uint32_t>(col0 >> 5) * 0x00010001u;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      const uint32_t chg = Pack2<T>::ne_mask(best[c], prev[c]);
+      chunk[c] = (cid2 & chg) | (chunk[c] & ~chg);
+    }
+  }
+  __device__ __forceinline__ void result(float& val, int& idx) const {
+    val = __int_as_float(0x7f800000);
+    idx = 0x7fffffff;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float v = e ? Pack2<T>::hi(best[c]) : Pack2<T>::lo(best[c]);
+        const uint32_t ch = e ? (chunk[c] >> 16) : (chunk[c] & 0xFFFFu);
+        const uint32_t lo = e ? (loc[c] >> 16) : (loc[c] & 0xFFFFu);
+        const int i = static_cast<int>((ch << 5) + (lo << 1)) + e;
+        if (v < val || (v == val && i < idx)) {
+          val = v;
+          idx = i;
+        }
+      }
+    }
+  }
+};
+
+template <typename T, int MODE>
+struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
+  float best[kChains];
+  int loc[kChains], chunk[kChains];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      best[c] = __int_as_float(0x7f800000);
+      loc[c] = 0;
+      chunk[c] = 0;
+    }
+  }
+  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const float* cs, float xsq,
+                                          int col0) {
+    float prev[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) prev[c] = best[c];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int c = j % kChains;
+      float cr = __uint_as_float(v[j]);
+      if constexpr (MODE == 1) cr = round16<T>(cr);
+      const float d = __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
+      const bool lt = d < best[c];
+      best[c] = fminf(best[c], d);
+      loc[c] = lt ? j : loc[c];
+    }
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) chunk[c] = (best[c] != prev[c]) ? (col0 >> 5) : chunk[c];
+  }
+  __device__ __forceinline__ void result(float& val, int& idx) const {
+    val = __int_as_float(0x7f800000);
+    idx = 0x7fffffff;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      const int i = (chunk[c] << 5) + loc[c];
+      if (best[c] < val || (best[c] == val && i < idx)) {
+        val = best[c];
+        idx = i;
+      }
+    }
+  }
+};
 
 // --------------------------------------------------------------------- kernel
 template <typename T, int MODE, bool XRES, int STAGES>
@@ -351,14 +475,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
       const bool valid = n < p.N;
       const float xsq_f = valid ? load_f(p.xsq, b * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
 
-      uint32_t best2 = 0, bloc = 0, bchunk = 0;  // mode 0 state
-      float bestf = __int_as_float(0x7f800000);  // modes 1/2 state
-      int bl = 0, bch = 0;
-      uint32_t xsq2 = 0;
-      if constexpr (MODE == 0) {
-        best2 = Pack2<T>::kInf2;
-        xsq2 = Pack2<T>::splat(xsq_f);  // exact: x_sq already holds a T value
-      }
+      using Argmin = typename std::conditional<MODE == 0, ArgminPacked<T>, ArgminF32<T, MODE>>::type;
+      Argmin am;
+      am.init();
+      uint32_t xsq2 = 0u;
+      if constexpr (MODE == 0) xsq2 = Pack2<T>::splat(xsq_f);  // exact: x_sq holds a T value
       const uint8_t* csq_row =
           static_cast<const uint8_t*>(p.csq) +
           static_cast<size_t>(b) * p.kpad * (MODE == 0 ? 2 : 4);
@@ -373,50 +494,35 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
         tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                static_cast<uint32_t>(ab * kCent + h * 128);
-#pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
+        // Four 32-column chunks; the TMEM load of chunk ch+1 is in flight while
+        // chunk ch is processed (va/vb alternate inside a two-chunk body).
+        auto process = [&](const uint32_t(&v)[32], int ch) {
           const int col0 = kt * kCent + h * 128 + ch * 32;
-          uint32_t v[32];
-          tmem_ld32(tbase + ch * 32, v);
           if constexpr (MODE == 0) {
             const uint4* cq = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
             uint4 c4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) c4[i] = __ldg(cq + i);
-            tmem_ld_wait(v);
-            const uint32_t* cw = reinterpret_cast<const uint32_t*>(c4);
-            const uint32_t prev = best2;
-#pragma unroll
-            for (int pp = 0; pp < 16; ++pp) {
-              const uint32_t d = Pack2<T>::dist(__uint_as_float(v[2 * pp]),
-                                                __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
-              const uint32_t m = Pack2<T>::lt_mask(d, best2);
-              best2 = (d & m) | (best2 & ~m);
-              bloc = ((static_cast<uint32_t>(pp) * 0x00010001u) & m) | (bloc & ~m);
-            }
-            const uint32_t chg = __vcmpne2(best2, prev);
-            const uint32_t cid2 = static_cast<uint32_t>(col0 >> 5) * 0x00010001u;
-            bchunk = (cid2 & chg) | (bchunk & ~chg);
+            am.chunk32(v, reinterpret_cast<const uint32_t*>(c4), xsq2, col0);
           } else {
             const float4* cq = reinterpret_cast<const float4*>(csq_row + col0 * 4);
             float4 c4[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) c4[i] = __ldg(cq + i);
-            tmem_ld_wait(v);
-            const float* cs = reinterpret_cast<const float*>(c4);
-            const float prev = bestf;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float cr = __uint_as_float(v[j]);
-              if constexpr (MODE == 1) cr = round16<T>(cr);
-              const float tt = __fmaf_rn(-2.0f, cr, xsq_f);
-              const float d = __fadd_rn(tt, cs[j]);
-              const bool lt = d < bestf;
-              bestf = lt ? d : bestf;
-              bl = lt ? j : bl;
-            }
-            bch = (bestf != prev) ? (col0 >> 5) : bch;
+            am.chunk32(v, reinterpret_cast<const float*>(c4), xsq_f, col0);
           }
+        };
+        uint32_t va[32], vb[32];
+        tmem_ld32(tbase, va);
+        tmem_ld_wait(va);
+#pragma unroll 1
+        for (int c2 = 0; c2 < 2; ++c2) {
+          tmem_ld32(tbase + (2 * c2 + 1) * 32, vb);
+          process(va, 2 * c2);
+          tmem_ld_wait(vb);
+          if (c2 == 0) tmem_ld32(tbase + 2 * 32, va);
+          process(vb, 2 * c2 + 1);
+          if (c2 == 0) tmem_ld_wait(va);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[ab]);
@@ -427,17 +533,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
       // Per-thread winner: (value, lowest column on ties).
       float val;
       int idx;
-      if constexpr (MODE == 0) {
-        const float ve = Pack2<T>::lo(best2), vo = Pack2<T>::hi(best2);
-        const int ie = static_cast<int>(((bchunk & 0xFFFFu) << 5) + ((bloc & 0xFFFFu) << 1));
-        const int io = static_cast<int>(((bchunk >> 16) << 5) + ((bloc >> 16) << 1) + 1);
-        const bool take_odd = (vo < ve) || (vo == ve && io < ie);
-        val = take_odd ? vo : ve;
-        idx = take_odd ? io : ie;
-      } else {
-        val = bestf;
-        idx = (bch << 5) + bl;
-      }
+      am.result(val, idx);
 
       // Merge the two column halves: half 1 publishes, half 0 decides.
       const int par = it & 1;
@@ -582,6 +678,23 @@ __global__ void prep_csq_kernel(const T* __restrict__ c, int64_t scb, int64_t sc
   }
 }
 
+// c_sq given: one thread per padded element (convert, +inf beyond K).
+template <typename T, int MODE>
+__global__ void copy_csq_kernel(const void* __restrict__ csq_in, int csq_dtype, int64_t sqb,
+                                int64_t sqk, void* __restrict__ csq_out, int64_t kpad, int K,
+                                int64_t total) {
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < total;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = r / kpad;
+    const int k = static_cast<int>(r % kpad);
+    const float v = k < K ? load_f(csq_in, b * sqb + k * sqk, csq_dtype) : __int_as_float(0x7f800000);
+    if (MODE == 0)
+      static_cast<T*>(csq_out)[r] = Elem<T>::from_f(v);
+    else
+      static_cast<float*>(csq_out)[r] = v;
+  }
+}
+
 template <typename T>
 static int assign_typed(const void* x, const void* cent, const void* x_sq, const void* c_sq,
                         int32_t* out, int32_t* counts, int xsq_dtype, int csq_dtype, int64_t B,
@@ -598,7 +711,18 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   const bool xres = is16 && nd <= kResidentChunks;
 
   // 1) padded c_sq in the distance dtype
-  {
+  if (c_sq) {
+    const int64_t total = B * kpad;
+    const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    if (mode == 0)
+      copy_csq_kernel<T, 0><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
+                                                         (int)K, total);
+    else
+      copy_csq_kernel<T, 1><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
+                                                         (int)K, total);
+    int st = check_launch("copy_csq_kernel");
+    if (st != FK_OK) return st;
+  } else {
     const int threads = 256;
     const int64_t rows = B * kpad;
     const int blocks = static_cast<int>(rows / 8 + 1 < 4096 ? rows / 8 + 1 : 4096);

@@ -91,110 +91,177 @@ __global__ void scatter_kernel(const I* __restrict__ ids, int64_t sib, int64_t s
   }
 }
 
+// 16-byte vector of T: raw load, then widen-and-add into float accumulators.
 template <typename T>
-struct Vec4Load;
-template <>
-struct Vec4Load<__half> {
-  __device__ __forceinline__ static void load(const __half* p, float (&v)[4]) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-    const __half2 a = *reinterpret_cast<const __half2*>(&u.x);
-    const __half2 c = *reinterpret_cast<const __half2*>(&u.y);
-    const float2 fa = __half22float2(a), fc = __half22float2(c);
-    v[0] = fa.x; v[1] = fa.y; v[2] = fc.x; v[3] = fc.y;
+struct Vec16 {
+  static constexpr int kElems = 16 / sizeof(T);
+  __device__ __forceinline__ static uint4 load(const T* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
   }
+  __device__ __forceinline__ static void add(float (&acc)[kElems], const uint4& u);
 };
 template <>
-struct Vec4Load<__nv_bfloat16> {
-  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[4]) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-    v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xFFFF0000u);
-    v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+__device__ __forceinline__ void Vec16<__half>::add(float (&acc)[8], const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    acc[2 * i] += f.x;
+    acc[2 * i + 1] += f.y;
   }
-};
+}
 template <>
-struct Vec4Load<float> {
-  __device__ __forceinline__ static void load(const float* p, float (&v)[4]) {
-    const float4 u = __ldg(reinterpret_cast<const float4*>(p));
-    v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+__device__ __forceinline__ void Vec16<__nv_bfloat16>::add(float (&acc)[8], const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc[2 * i] += __uint_as_float(w[i] << 16);
+    acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
   }
-};
+}
+template <>
+__device__ __forceinline__ void Vec16<float>::add(float (&acc)[4], const uint4& u) {
+  acc[0] += __uint_as_float(u.x);
+  acc[1] += __uint_as_float(u.y);
+  acc[2] += __uint_as_float(u.z);
+  acc[3] += __uint_as_float(u.w);
+}
 
 constexpr int kSegWarps = 8;
-constexpr int kSegSlice = 128;  // columns per warp slice (32 lanes x 4)
+constexpr int kSegPos = 64;    // sorted positions per warp
+constexpr int kSegUnroll = 8;  // rows per lane group loaded before use
 
-__device__ __forceinline__ void flush_run(float* sums, int64_t rowbase, int d0, int D, bool vec,
-                                          const float (&acc)[4]) {
-  float* dst = sums + rowbase + d0;
-  if (vec && d0 + 4 <= D) {
-    atomicAdd(reinterpret_cast<float4*>(dst), make_float4(acc[0], acc[1], acc[2], acc[3]));
+template <int E>
+__device__ __forceinline__ void flush_run(float* dst, int d0, int D, bool vec, const float (&acc)[E]) {
+  if (vec && d0 + E <= D) {
+#pragma unroll
+    for (int i = 0; i < E; i += 4)
+      atomicAdd(reinterpret_cast<float4*>(dst + i),
+                make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
   } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+    for (int e = 0; e < E; ++e)
       if (d0 + e < D) atomicAdd(dst + e, acc[e]);
   }
 }
 
-// grid (ceil(N / 256), column slices, B); block = 8 warps x 32 sorted points.
-template <typename T, bool VLOAD>
-__global__ void segsum_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
-                              const int32_t* __restrict__ perm, const int32_t* __restrict__ sid,
-                              const int32_t* __restrict__ offs, const int32_t* __restrict__ hist,
-                              int N, int K, int D, float* __restrict__ sums, bool vflush) {
+// grid (ceil(N / (8 warps * 64)), column slices, B).  A warp walks 64
+// consecutive sorted points.  Its lanes form 32/L groups of L lanes; a group
+// owns a contiguous share of the 64 points and reads each row slice as L
+// 16-byte vectors, so one load instruction fetches 32/L rows and
+// kSegUnroll instructions are in flight before any value is used.  Runs of
+// equal labels are summed in registers and flushed with vector atomics.
+// Rows must be 16-byte aligned; columns past D inside the last vector are
+// read (row padding) but never stored.
+template <typename T, int L>
+__global__ void __launch_bounds__(kSegWarps * 32)
+    segsum_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn,
+                  const int32_t* __restrict__ perm, const int32_t* __restrict__ sid,
+                  const int32_t* __restrict__ offs, const int32_t* __restrict__ hist, int N, int K,
+                  int D, float* __restrict__ sums, bool vflush) {
+  constexpr int E = Vec16<T>::kElems;
+  constexpr int G = 32 / L;          // row groups per warp
+  constexpr int PG = kSegPos / G;    // points per group
   const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t hb = static_cast<int64_t>(b) * K;
   const int total_b = offs[hb + K - 1] + hist[hb + K - 1];
-  const int p0 = blockIdx.x * (kSegWarps * 32) + warp * 32;
+  const int p0 = blockIdx.x * (kSegWarps * kSegPos) + warp * kSegPos;
   if (p0 >= total_b) return;
-  const int np = min(32, total_b - p0);
-  int my_n = 0, my_id = -1;
-  if (lane < np) {
-    my_n = perm[static_cast<int64_t>(b) * N + p0 + lane];
-    my_id = sid[static_cast<int64_t>(b) * N + p0 + lane];
-  }
-  const int d0 = blockIdx.y * kSegSlice + lane * 4;
+  const int np = min(kSegPos, total_b - p0);
+  const int64_t pb = static_cast<int64_t>(b) * N + p0;
+  int my_n0 = 0, my_n1 = 0, my_i0 = -1, my_i1 = -1;
+  if (lane < np) { my_n0 = __ldg(perm + pb + lane); my_i0 = __ldg(sid + pb + lane); }
+  if (lane + 32 < np) { my_n1 = __ldg(perm + pb + lane + 32); my_i1 = __ldg(sid + pb + lane + 32); }
+  const int g = lane / L;
+  const int d0 = blockIdx.y * (L * E) + (lane % L) * E;
   const bool lane_active = d0 < D;
+  const int ng = max(0, min(PG, np - g * PG));  // points of this lane's group
   const T* xb = x + b * sxb;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int cur = __shfl_sync(0xffffffffu, my_id, 0);
-  for (int i = 0; i < np; i += 4) {
-    float v[4][4];
+  auto fetch = [&](int q, int a0, int a1) {  // value of position q from a per-lane pair
+    const int s0 = __shfl_sync(0xffffffffu, a0, q & 31);
+    const int s1 = __shfl_sync(0xffffffffu, a1, q & 31);
+    return (q >> 5) ? s1 : s0;
+  };
+  float acc[E];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int n = __shfl_sync(0xffffffffu, my_n, (i + u) & 31);
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  int cur = fetch(g * PG, my_i0, my_i1);
+  const int steps = min(PG, np);  // group 0 has the most points
+  for (int j0 = 0; j0 < steps; j0 += kSegUnroll) {
+    uint4 v[kSegUnroll];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[u][e] = 0.f;
-      if (i + u < np && lane_active) {
-        const T* row = xb + static_cast<int64_t>(n) * sxn;
-        if (VLOAD && d0 + 4 <= D) {
-          Vec4Load<T>::load(row + d0, v[u]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (d0 + e < D) v[u][e] = Elem<T>::to_f(row[static_cast<int64_t>(d0 + e) * sxd]);
-        }
-      }
+    for (int u = 0; u < kSegUnroll; ++u) {
+      const int j = j0 + u;
+      const int n = fetch(g * PG + (j < PG ? j : 0), my_n0, my_n1);
+      v[u] = (j < ng && lane_active) ? Vec16<T>::load(xb + static_cast<int64_t>(n) * sxn + d0)
+                                     : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (i + u < np) {  // warp-uniform
-        const int id = __shfl_sync(0xffffffffu, my_id, i + u);
+    for (int u = 0; u < kSegUnroll; ++u) {
+      const int j = j0 + u;
+      const int id = fetch(g * PG + (j < PG ? j : 0), my_i0, my_i1);
+      if (j < ng) {
         if (id != cur) {
-          if (lane_active) flush_run(sums, (hb + cur) * D, d0, D, vflush, acc);
+          if (lane_active) flush_run<E>(sums + (hb + cur) * D + d0, d0, D, vflush, acc);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[e] = 0.f;
+          for (int e = 0; e < E; ++e) acc[e] = 0.f;
           cur = id;
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] += v[u][e];
+        Vec16<T>::add(acc, v[u]);
       }
     }
   }
-  if (lane_active) flush_run(sums, (hb + cur) * D, d0, D, vflush, acc);
+  if (ng > 0 && lane_active) flush_run<E>(sums + (hb + cur) * D + d0, d0, D, vflush, acc);
+}
+
+// Fallback for rows that are not 16-byte aligned: one warp per 64 points,
+// lane = column (strided), scalar loads.
+template <typename T>
+__global__ void __launch_bounds__(kSegWarps * 32)
+    segsum_scalar_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
+                         const int32_t* __restrict__ perm, const int32_t* __restrict__ sid,
+                         const int32_t* __restrict__ offs, const int32_t* __restrict__ hist, int N,
+                         int K, int D, float* __restrict__ sums) {
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t hb = static_cast<int64_t>(b) * K;
+  const int total_b = offs[hb + K - 1] + hist[hb + K - 1];
+  const int p0 = blockIdx.x * (kSegWarps * kSegPos) + warp * kSegPos;
+  if (p0 >= total_b) return;
+  const int np = min(kSegPos, total_b - p0);
+  const int64_t pb = static_cast<int64_t>(b) * N + p0;
+  const T* xb = x + b * sxb;
+  for (int d = blockIdx.y * 32 + lane; d < D; d += 32 * gridDim.y) {
+    float acc = 0.f;
+    int cur = __ldg(sid + pb);
+    for (int j = 0; j < np; ++j) {
+      const int id = __ldg(sid + pb + j);
+      if (id != cur) {
+        atomicAdd(sums + (hb + cur) * D + d, acc);
+        acc = 0.f;
+        cur = id;
+      }
+      acc += Elem<T>::to_f(xb[static_cast<int64_t>(__ldg(perm + pb + j)) * sxn + d * sxd]);
+    }
+    atomicAdd(sums + (hb + cur) * D + d, acc);
+  }
 }
 
 // One warp per (b, k): reference finalize (centroid_update_triton.py:378-385,
-// torch_fallback.py:101-108) plus ||c_new||^2 and the shift.
+// torch_fallback.py:101-108) plus ||c_new||^2 and the shift.  Lane l owns
+// columns 4l..4l+3 of every 128-column slice (float4 loads of the sums).
+template <typename T>
+__device__ __forceinline__ void fin_elem(float sumv, int32_t cnt, float fc, T ov, T* dst,
+                                         float& ss, float& cs) {
+  const T nv = cnt > 0 ? Elem<T>::from_f(sumv / fc) : ov;
+  *dst = nv;
+  const float nf = Elem<T>::to_f(nv);
+  const float df = Elem<T>::round(nf - Elem<T>::to_f(ov));
+  ss += df * df;
+  cs += Elem<T>::round(nf * nf);
+}
+
 template <typename T>
 __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ counts,
                                 const T* __restrict__ old, int64_t sob, int64_t sok, int64_t sod,
@@ -204,6 +271,8 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
   const int wpb = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t rows = static_cast<int64_t>(B) * K;
+  const bool vec = (D % 4 == 0) && sod == 1 && snd == 1;
+  float wmax = 0.f;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); r < rows;
        r += static_cast<int64_t>(gridDim.x) * wpb) {
     const int64_t b = r / K, k = r % K;
@@ -213,26 +282,37 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
     const T* o = old + b * sob + k * sok;
     T* nw = out + b * snb + k * snk;
     float ss = 0.f, cs = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const T ov = o[d * sod];
-      const T nv = cnt > 0 ? Elem<T>::from_f(s[d] / fc) : ov;
-      if (reset) s[d] = 0.f;
-      nw[d * snd] = nv;
-      const float nf = Elem<T>::to_f(nv);
-      const float df = Elem<T>::round(nf - Elem<T>::to_f(ov));
-      ss += df * df;
-      cs += Elem<T>::round(nf * nf);
+    if (vec) {
+      for (int d = lane * 4; d < D; d += 128) {
+        const float4 sv = *reinterpret_cast<const float4*>(s + d);
+        if (reset) *reinterpret_cast<float4*>(s + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float svs[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) fin_elem<T>(svs[e], cnt, fc, o[d + e], nw + d + e, ss, cs);
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) {
+        const float sv = s[d];
+        if (reset) s[d] = 0.f;
+        fin_elem<T>(sv, cnt, fc, o[d * sod], nw + d * snd, ss, cs);
+      }
     }
     ss = warp_sum(ss);
     cs = warp_sum(cs);
     if (reset && lane == 0) counts[r] = 0;
     if (lane == 0) {
       if (csq_out) csq_out[r] = Elem<T>::round(cs);
-      if (shift_out) {
-        const float sh = Elem<T>::round(sqrtf(ss));
-        atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(sh));
-      }
+      wmax = fmaxf(wmax, Elem<T>::round(sqrtf(ss)));
     }
+  }
+  // one atomic per block for the shift (non-negative floats order as uints)
+  __shared__ float blk_max[32];
+  if (lane == 0) blk_max[threadIdx.x >> 5] = wmax;
+  __syncthreads();
+  if (threadIdx.x == 0 && shift_out) {
+    float m = 0.f;
+    for (int w = 0; w < wpb; ++w) m = fmaxf(m, blk_max[w]);
+    atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(m));
   }
 }
 
@@ -265,24 +345,42 @@ static int hist_scatter(const void* ids, const int64_t* is, int64_t B, int64_t N
   return check_launch("scatter_kernel");
 }
 
+template <typename T, int L>
+static void launch_segsum(const T* x, const int64_t* xs, int64_t B, int64_t N, int64_t K, int64_t D,
+                          const int32_t* perm, const int32_t* sid, const int32_t* offs,
+                          const int32_t* hist, float* sums, bool vflush, cudaStream_t s) {
+  constexpr int E = 16 / sizeof(T);
+  dim3 grid(static_cast<unsigned>((N + kSegWarps * kSegPos - 1) / (kSegWarps * kSegPos)),
+            static_cast<unsigned>((D + L * E - 1) / (L * E)), static_cast<unsigned>(B));
+  segsum_kernel<T, L><<<grid, kSegWarps * 32, 0, s>>>(x, xs[0], xs[1], perm, sid, offs, hist,
+                                                      (int)N, (int)K, (int)D, sums, vflush);
+}
+
 template <typename T>
 static int segsum_typed(const void* x, const int64_t* xs, int64_t B, int64_t N, int64_t K,
                         int64_t D, const int32_t* perm, const int32_t* sid, const int32_t* offs,
                         const int32_t* hist, float* sums, cudaStream_t s) {
+  constexpr int E = 16 / sizeof(T);
   const bool vload = xs[2] == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                      ((xs[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0) &&
-                     ((xs[0] * static_cast<int64_t>(sizeof(T))) % 16 == 0 || B == 1);
+                     ((xs[0] * static_cast<int64_t>(sizeof(T))) % 16 == 0 || B == 1) &&
+                     xs[1] >= (D + E - 1) / E * E;
   const bool vflush = (D % 4 == 0) && (reinterpret_cast<uintptr_t>(sums) % 16 == 0);
-  dim3 grid(static_cast<unsigned>((N + kSegWarps * 32 - 1) / (kSegWarps * 32)),
-            static_cast<unsigned>((D + kSegSlice - 1) / kSegSlice), static_cast<unsigned>(B));
-  if (vload)
-    segsum_kernel<T, true><<<grid, kSegWarps * 32, 0, s>>>(static_cast<const T*>(x), xs[0], xs[1],
-                                                           xs[2], perm, sid, offs, hist, (int)N,
-                                                           (int)K, (int)D, sums, vflush);
-  else
-    segsum_kernel<T, false><<<grid, kSegWarps * 32, 0, s>>>(static_cast<const T*>(x), xs[0], xs[1],
-                                                            xs[2], perm, sid, offs, hist, (int)N,
-                                                            (int)K, (int)D, sums, vflush);
+  const T* xt = static_cast<const T*>(x);
+  if (vload) {
+    const int64_t vecs = (D + E - 1) / E;  // 16-byte vectors per row
+    if (vecs <= 8)
+      launch_segsum<T, 8>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
+    else if (vecs <= 16)
+      launch_segsum<T, 16>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
+    else
+      launch_segsum<T, 32>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
+  } else {
+    dim3 grid(static_cast<unsigned>((N + kSegWarps * kSegPos - 1) / (kSegWarps * kSegPos)),
+              static_cast<unsigned>(D > 32 * 16 ? 16 : (D + 31) / 32), static_cast<unsigned>(B));
+    segsum_scalar_kernel<T><<<grid, kSegWarps * 32, 0, s>>>(xt, xs[0], xs[1], xs[2], perm, sid,
+                                                           offs, hist, (int)N, (int)K, (int)D, sums);
+  }
   return check_launch("segsum_kernel");
 }
 

@@ -189,10 +189,11 @@ class _DeviceLane:
         self.c_cur, self.c_nxt = self.c_nxt, self.c_cur
 
     def read_stat(self):
+        """(shift, device status) after the work queued on the compute stream."""
         host = torch.empty(4, dtype=torch.int32, pin_memory=True)
-        with torch.cuda.device(self.dev):
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.compute_stream):
             host.copy_(self.stat, non_blocking=True)
-            self.compute_stream.synchronize()
+        self.compute_stream.synchronize()
         return host[0:1].view(torch.float32).item(), int(host[1].item())
 
 

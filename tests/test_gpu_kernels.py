@@ -45,7 +45,8 @@ def test_row_sqnorm_matches_oracle(fk, dt, D):
     rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-6)
     ulp = {"float16": 2 ** -10, "bfloat16": 2 ** -7, "float32": 1e-5}[dt]
     assert rel.max() <= ulp * 1.01
-    assert (got != want).mean() < 0.02
+    if dt != "float32":  # 16-bit results are rounded once: nearly always identical
+        assert (got != want).mean() < 0.02
 
 
 # ----------------------------------------------------------------- assignment

@@ -168,11 +168,18 @@ def test_kmeans_largeN_single_gpu_vs_oracle(fk):
 
 
 def test_kmeans_largeN_tol_break_returns_new_centroids(fk):
+    """On a tolerance break kmeans_largeN returns the centroids UPDATED from the
+    returned labels (kmeans_large.py:251-258), unlike batch_kmeans_Euclid."""
     rng = np.random.default_rng(8)
     x = ko.gmm_points(rng, 1, 50_000, 16, 8, 6.0)[0]
     c0 = x[rng.integers(0, len(x), 8)]
     labels, cent = fk.kmeans_largeN(torch.from_numpy(x), 8, max_iters=100, tol=1e-3,
                                     BLOCK_N=16_384, init_centroids=torch.from_numpy(c0),
                                     device="cuda:0")
-    o_ids, o_cent = ko.kmeans_large_n(x, 8, 100, 1e-3, init_centroids=c0, dtype="float32")
-    np.testing.assert_allclose(_np(cent), o_cent, rtol=1e-4, atol=1e-4)
+    lab = labels.cpu().numpy()
+    # the returned centroids are the means of the returned labelling ...
+    upd = ko.centroid_update(x[None], lab[None], _np(cent)[None], "float32", exact_order=False)
+    assert_centroids(_np(cent)[None], upd, "centroids are the update of the labels", rtol=1e-5)
+    # ... and the run had converged: one more assignment barely moves anything
+    again = ko.assign(x[None], _np(cent)[None], ko.row_sqnorm(x[None], "float32"), "float32")[0]
+    assert (again == lab).mean() > 0.999
