@@ -28,6 +28,7 @@
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
 // centroid chunk instead of staying resident.
+#include <mutex>
 #include <type_traits>
 
 #include "fk_common.cuh"
@@ -848,4 +849,83 @@ extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq,
                                  K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
                                  out_strides2, workspace, dev_status, s);
   }
+}
+
+// ---------------------------------------------------------------------------
+// fk_assign_static_scratch: fk_assign for callers that cannot allocate.
+//
+// Some hosts hand a plugin only its input and output buffers: an inference
+// server's custom-op interface with no workspace hook, a framework whose
+// memory pool forbids side allocations, or a latency-bound loop where
+// cudaMalloc/cudaFree (which can synchronise the device) is not acceptable.
+// This entry point needs no caller workspace: its scratch (the padded
+// per-centroid squared norms, B * ceil(K/256)*256 * 4 bytes plus 256) lives
+// in the file-scope device array below, which every GPU that loads this
+// library holds until the process exits.
+//
+// * Limit: kAssignStaticScratchBytes = 1 MiB, i.e. B * ceil(K/256)*256 <= 262080
+//   (for example B=32 with K <= 8192, or B=1 with K <= 262080); larger
+//   problems are rejected with FK_ERR_WORKSPACE before anything is launched.
+// * The first call on a device looks up the array's device address for that
+//   device (cudaGetSymbolAddress, with that device current); make that first
+//   call before any stream capture.
+// * All calls on a device share the one array and it keeps the last call's
+//   contents; every call rewrites all the scratch it reads, so nothing needs
+//   clearing, but calls that overlap on the GPU (different streams, or
+//   different host threads on the same device) race on it.
+// * No cudaMalloc, cudaFree or allocating library routine is called.
+// ---------------------------------------------------------------------------
+namespace fk {
+
+constexpr size_t kAssignStaticScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) uint8_t g_assign_static_scratch[kAssignStaticScratchBytes];
+
+struct StaticScratchSlot {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+static StaticScratchSlot g_static_scratch_slots[64];
+
+static int static_scratch_for_current_device(void** out) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "fk_assign_static_scratch: bad current device");
+  StaticScratchSlot& slot = g_static_scratch_slots[dev];
+  std::call_once(slot.once, [&slot] {
+    // runs with `dev` current: the caller's current device is this slot's device
+    slot.err = cudaGetSymbolAddress(&slot.ptr, g_assign_static_scratch);
+  });
+  if (slot.err != cudaSuccess || slot.ptr == nullptr)
+    return fail(FK_ERR_CUDA, "fk_assign_static_scratch: cudaGetSymbolAddress failed on device %d: %s",
+                dev, cudaGetErrorString(slot.err));
+  *out = slot.ptr;
+  return FK_OK;
+}
+
+}  // namespace fk
+
+extern "C" int fk_assign_static_scratch(const void* x, const void* centroids, const void* x_sq,
+                                        const void* c_sq, int32_t* out, int32_t* counts,
+                                        int dtype, int xsq_dtype, int csq_dtype, int64_t B,
+                                        int64_t N, int64_t K, int64_t D,
+                                        const int64_t* x_strides3, const int64_t* c_strides3,
+                                        const int64_t* xsq_strides2, const int64_t* csq_strides2,
+                                        const int64_t* out_strides2, int32_t* dev_status,
+                                        void* stream) {
+  if (B < 0 || N < 0 || K <= 0 || D <= 0)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_static_scratch: bad sizes B=%lld N=%lld K=%lld D=%lld",
+                (long long)B, (long long)N, (long long)K, (long long)D);
+  if (B == 0 || N == 0) return FK_OK;
+  const size_t need = fk_assign_workspace_size(B, K, dtype);
+  if (need > kAssignStaticScratchBytes)
+    return fail(FK_ERR_WORKSPACE,
+                "fk_assign_static_scratch: B=%lld, K=%lld needs %zu bytes of scratch; the static "
+                "scratch holds %zu (B * ceil(K/256)*256 <= 262080); use fk_assign with a workspace",
+                (long long)B, (long long)K, need, kAssignStaticScratchBytes);
+  void* scratch = nullptr;
+  const int st = static_scratch_for_current_device(&scratch);
+  if (st != FK_OK) return st;
+  return fk_assign(x, centroids, x_sq, c_sq, out, counts, dtype, xsq_dtype, csq_dtype, B, N, K, D,
+                   x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2, scratch,
+                   kAssignStaticScratchBytes, dev_status, stream);
 }

@@ -105,6 +105,25 @@ int fk_assign(const void* x, const void* centroids, const void* x_sq, const void
               const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
               size_t workspace_bytes, int32_t* dev_status, void* stream);
 
+/* fk_assign for callers that cannot allocate (no counterpart in the reference).
+ * Some hosts give a plugin only its inputs and outputs: a serving framework's
+ * custom-op interface without a workspace hook, a memory pool that forbids side
+ * allocations, or a latency-bound loop where cudaMalloc/cudaFree (which can
+ * synchronise the device) is not acceptable.  Same arguments and results as
+ * fk_assign, minus the workspace: the scratch is a 1 MiB file-scope device
+ * array that every GPU loading this library keeps until exit.
+ * Limit: B * ceil(K/256)*256 <= 262080 (e.g. B=32, K <= 8192); larger sizes
+ * return FK_ERR_WORKSPACE.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All
+ * calls on a device share the array (each call rewrites what it reads);
+ * calls that overlap on the GPU race on it.  Allocates nothing. */
+int fk_assign_static_scratch(const void* x, const void* centroids, const void* x_sq,
+                             const void* c_sq, int32_t* out, int32_t* counts, int dtype,
+                             int xsq_dtype, int csq_dtype, int64_t B, int64_t N, int64_t K,
+                             int64_t D, const int64_t* x_strides3, const int64_t* c_strides3,
+                             const int64_t* xsq_strides2, const int64_t* csq_strides2,
+                             const int64_t* out_strides2, int32_t* dev_status, void* stream);
+
 /* Per-cluster float32 sums (B,K,D contiguous) and int32 counts (B,K contiguous)
  * of the rows of x grouped by ids (B,N; FK_I32 or FK_I64), ADDED to `sums`
  * and `counts`.  `hist` (B,K) optional: the histogram of exactly these ids
