@@ -47,11 +47,12 @@ constexpr int kConvWarp0 = 10;
 constexpr int kConvWarps = 4;
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
 
-template <int MODE, bool XRES, int STAGES>
+template <int MODE, bool XRES, int STAGES, bool FUSE = false>
 struct Layout {
   static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
+  static constexpr int XB = FUSE ? 3 : 2;              // resident x tile buffers
   static constexpr int x_off = 0;
-  static constexpr int x_bytes = XRES ? 2 * kResidentChunks * kXChunk : 0;
+  static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
   static constexpr int st_clo = kCChunk;                  // centroid chunk lo (mode 2)
   static constexpr int st_x = kCChunk * kSplit;           // x chunk (split-D)
@@ -60,13 +61,15 @@ struct Layout {
   static constexpr int stages_off = x_off + x_bytes;
   static constexpr int merge_off = stages_off + STAGES * stage_bytes;
   static constexpr int merge_bytes = 2 * kRows * 8;     // [parity][row] (value, index)
-  static constexpr int bar_off = merge_off + merge_bytes;
-  // x_full[2] x_empty[2] c_full[S] c_empty[S] conv_full[S] acc_full[2] acc_empty[2]
-  // merge_full[2] merge_empty[2] final[1]
-  static constexpr int nbars = 4 + 3 * STAGES + 4 + 4 + 1;
+  static constexpr int lab_off = merge_off + merge_bytes;
+  static constexpr int lab_bytes = FUSE ? 2 * kRows * 4 : 0;  // [parity][row] label or -1
+  static constexpr int bar_off = lab_off + lab_bytes;
+  // x_full[3] x_empty[3] c_full[S] c_empty[S] conv_full[S] acc_full[2] acc_empty[2]
+  // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
+  static constexpr int nbars = 6 + 3 * STAGES + 4 + 4 + 4 + 1;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
-  static constexpr int threads = (MODE == 2 ? 14 : 10) * 32;
+  static constexpr int threads = ((MODE == 2 || FUSE) ? 14 : 10) * 32;
 };
 
 struct AssignParams {
@@ -78,6 +81,9 @@ struct AssignParams {
   int32_t* out;
   int64_t so_b, so_n;
   int32_t* counts;  // (B, K) or null
+  float* sums;      // (B, K, D) contiguous, only with FUSE
+  int D;
+  bool sums_vec;    // D % 4 == 0 and 16-byte aligned sums: float4 atomics
   int N, K;
   int nd;           // 128-byte column chunks per row
   int dch;          // elements per chunk
@@ -278,11 +284,11 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
 };
 
 // --------------------------------------------------------------------- kernel
-template <typename T, int MODE, bool XRES, int STAGES>
-__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
+template <typename T, int MODE, bool XRES, int STAGES, bool FUSE>
+__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
     assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
-  using L = Layout<MODE, XRES, STAGES>;
+  using L = Layout<MODE, XRES, STAGES, FUSE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -292,22 +298,30 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar_off);
   uint64_t* x_full = bars;
-  uint64_t* x_empty = bars + 2;
-  uint64_t* c_full = bars + 4;
+  uint64_t* x_empty = bars + 3;
+  uint64_t* c_full = bars + 6;
   uint64_t* c_empty = c_full + STAGES;
   uint64_t* conv_full = c_empty + STAGES;
   uint64_t* acc_full = conv_full + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* merge_full = acc_empty + 2;
   uint64_t* merge_empty = merge_full + 2;
-  uint64_t* final_bar = merge_empty + 2;
+  uint64_t* lab_full = merge_empty + 2;
+  uint64_t* lab_empty = lab_full + 2;
+  uint64_t* final_bar = lab_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);
+      // with FUSE the resident x tile is also read by the 128 sum threads
+      // (the points' rows) before it may be overwritten
+      mbar_init(&x_empty[i], FUSE ? 1 + 128 : 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&lab_full[i], 128);
+      mbar_init(&lab_empty[i], 128);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps * 32);
       mbar_init(&merge_full[i], 4 * 32);
@@ -344,7 +358,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
       uint32_t xph = 0;
       int last_par[STAGES];
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
-      int last_xpar[2] = {-1, -1};
+      int last_xpar[3] = {-1, -1, -1};
       bool ok = true;
       for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
         const int b = t / p.ntn;
@@ -359,7 +373,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
             tma_load_3d(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk, &tmap_x,
                         &x_full[xb], dc * p.dch, row0, b);
           last_xpar[xb] = static_cast<int>(xph);
-          if (++xb == 2) { xb = 0; xph ^= 1; }
+          if (++xb == L::XB) { xb = 0; xph ^= 1; }
         }
         for (int kt = 0; ok && kt < p.nkt; ++kt) {
           for (int dc = 0; dc < p.nd; ++dc) {
@@ -381,7 +395,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
         // Let every load already issued land before the CTA can exit.
         for (int s = 0; s < STAGES; ++s)
           if (last_par[s] >= 0) drain_wait(&c_full[s], static_cast<uint32_t>(last_par[s]), 200000000ull);
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < L::XB; ++i)
           if (last_xpar[i] >= 0) drain_wait(&x_full[i], static_cast<uint32_t>(last_xpar[i]), 200000000ull);
       }
     }
@@ -451,7 +465,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
         if constexpr (XRES) {
           if (ok) {
             mma_commit(&x_empty[xb]);
-            if (++xb == 2) { xb = 0; xph ^= 1; }
+            if (++xb == L::XB) { xb = 0; xph ^= 1; }
           }
         }
       }
@@ -566,7 +580,69 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
           p.out[b * p.so_b + static_cast<int64_t>(n) * p.so_n] = idx;
           if (p.counts) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
         }
+        if constexpr (FUSE && XRES) {
+          // hand the label (or -1 past N) to the sum warps
+          const bool got2 = mbar_wait(&lab_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got2)) {
+            ok = false;
+            break;
+          }
+          reinterpret_cast<int*>(smem + L::lab_off)[par * kRows + row] = valid ? idx : -1;
+          mbar_arrive(&lab_full[par]);
+        }
       }
+    }
+  } else if (FUSE && XRES) {
+    // ------------------------------------------- sum warps (fused accumulation)
+    // Thread s owns row s of every tile: once the epilogue has published the
+    // tile's labels, it adds its row (still resident in the tile's x buffer,
+    // 128-byte swizzle: 16-byte unit u of row r at r*128 + ((u ^ (r % 8)) * 16)
+    // of each 64-column chunk) to sums[label] with float4 atomics, then
+    // releases the x buffer.  Runs concurrently with the next tile's epilogue.
+    if constexpr (FUSE && XRES && sizeof(T) == 2) {
+    const int srow = threadIdx.x - kConvWarp0 * 32;  // 0..127
+    int it = 0, xi = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++it) {
+      const int b = t / p.ntn;
+      const int par = it & 1;
+      const uint32_t mph = static_cast<uint32_t>((it >> 1) & 1);
+      const bool got = mbar_wait(&lab_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const int lab = reinterpret_cast<const int*>(smem + L::lab_off)[par * kRows + srow];
+      mbar_arrive(&lab_empty[par]);
+      if (lab >= 0) {
+        float* dst = p.sums + (static_cast<int64_t>(b) * p.K + lab) * p.D;
+        const uint8_t* xbuf = smem + L::x_off + xi * kResidentChunks * kXChunk;
+        for (int dc = 0; dc < p.nd; ++dc) {
+          const uint8_t* seg = xbuf + dc * kXChunk + srow * kChunkB;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int col = dc * p.dch + u * 8;
+            if (col < p.D) {
+              const uint4 q4 = *reinterpret_cast<const uint4*>(seg + ((u ^ (srow & 7)) * 16));
+              const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                f[2 * e] = Pack2<T>::lo(w4[e]);
+                f[2 * e + 1] = Pack2<T>::hi(w4[e]);
+              }
+              if (p.sums_vec && col + 8 <= p.D) {
+                atomicAdd(reinterpret_cast<float4*>(dst + col), make_float4(f[0], f[1], f[2], f[3]));
+                atomicAdd(reinterpret_cast<float4*>(dst + col + 4), make_float4(f[4], f[5], f[6], f[7]));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (col + e < p.D) atomicAdd(dst + col + e, f[e]);
+              }
+            }
+          }
+        }
+      }
+      mbar_arrive(&x_empty[xi]);
+      if (++xi == L::XB) xi = 0;
+    }
     }
   } else if (MODE == 2) {
     // ---------------------------------------- 3xTF32 split converters (mode 2)
@@ -619,13 +695,13 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES>::threads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-template <typename T, int MODE, bool XRES>
+template <typename T, int MODE, bool XRES, bool FUSE = false>
 static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
                          cudaStream_t stream) {
-  constexpr int STAGES = (MODE == 2) ? 2 : 4;
-  using L = Layout<MODE, XRES, STAGES>;
+  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : 4);
+  using L = Layout<MODE, XRES, STAGES, FUSE>;
   static_assert(L::total <= 232448, "shared memory budget");
-  auto kern = assign_kernel<T, MODE, XRES, STAGES>;
+  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE>;
   const int dev = current_device();
   static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);
@@ -701,7 +777,7 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
                         int32_t* out, int32_t* counts, int xsq_dtype, int csq_dtype, int64_t B,
                         int64_t N, int64_t K, int64_t D, const int64_t* xs, const int64_t* cs,
                         const int64_t* xqs, const int64_t* cqs, const int64_t* os, void* ws,
-                        int32_t* status, cudaStream_t stream) {
+                        int32_t* status, cudaStream_t stream, float* sums = nullptr) {
   constexpr int eb = Elem<T>::kBytes;
   const bool is16 = eb == 2;
   const int mode = is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2;
@@ -762,6 +838,9 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.so_b = os[0];
   p.so_n = os[1];
   p.counts = counts;
+  p.sums = sums;
+  p.D = static_cast<int>(D);
+  p.sums_vec = (D % 4 == 0) && (reinterpret_cast<uintptr_t>(sums) % 16 == 0);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.nd = nd;
@@ -772,6 +851,11 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.status = status;
 
   if constexpr (Elem<T>::kBytes == 2) {
+    if (sums) {  // fused centroid sums: resident x tiles only (checked by the caller)
+      if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
+      return mode == 0 ? launch_assign<T, 0, true, true>(tx, tc, p, stream)
+                       : launch_assign<T, 1, true, true>(tx, tc, p, stream);
+    }
     if (mode == 0) return xres ? launch_assign<T, 0, true>(tx, tc, p, stream)
                                : launch_assign<T, 0, false>(tx, tc, p, stream);
     return xres ? launch_assign<T, 1, true>(tx, tc, p, stream)
@@ -849,6 +933,90 @@ extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq,
                                  K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
                                  out_strides2, workspace, dev_status, s);
   }
+}
+
+// ---------------------------------------------------------------------------
+// fk_assign_accumulate: assignment plus centroid sums/counts in one pass.
+// 16-bit x with D <= 128 (x tile resident in shared memory): one kernel; each
+// point's row is added to sums[label] right after its label is decided, so x
+// is read once per Lloyd iteration.  Other layouts: fk_assign with a workspace
+// histogram followed by fk_centroid_accumulate (counting-sort path).
+// ---------------------------------------------------------------------------
+static bool assign_accumulate_fused(int64_t D, int dtype) {
+  if (dtype != FK_F16 && dtype != FK_BF16) return false;
+  const int64_t nd = (D * 2 + kChunkB - 1) / kChunkB;
+  return nd <= kResidentChunks;
+}
+
+extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
+                                                      int dtype) {
+  const size_t wa = fk_assign_workspace_size(B, K, dtype);
+  if (assign_accumulate_fused(D, dtype)) return wa;
+  return wa + align_up(static_cast<size_t>(B > 0 && K > 0 ? B * K : 1) * 4, 256) +
+         fk_centroid_accumulate_workspace_size(B, N, K);
+}
+
+extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq,
+                                    const void* c_sq, int32_t* out, int32_t* counts, float* sums,
+                                    int dtype, int xsq_dtype, int csq_dtype, int64_t B, int64_t N,
+                                    int64_t K, int64_t D, const int64_t* x_strides3,
+                                    const int64_t* c_strides3, const int64_t* xsq_strides2,
+                                    const int64_t* csq_strides2, const int64_t* out_strides2,
+                                    void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                    void* stream) {
+  if (!counts || !sums) return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: counts and sums are required");
+  if (B < 0 || N < 0 || K <= 0 || D <= 0)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: bad sizes");
+  if (B == 0 || N == 0) return FK_OK;
+  const size_t need = fk_assign_accumulate_workspace_size(B, N, K, D, dtype);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FK_ERR_WORKSPACE, "fk_assign_accumulate: workspace needs %zu bytes, 256-aligned", need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!assign_accumulate_fused(D, dtype)) {
+    const size_t wa = fk_assign_workspace_size(B, K, dtype);
+    int32_t* hist = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + wa);
+    void* wu = static_cast<uint8_t*>(workspace) + wa + align_up(static_cast<size_t>(B * K) * 4, 256);
+    cudaError_t e = cudaMemsetAsync(hist, 0, static_cast<size_t>(B * K) * 4, s);
+    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    int st = fk_assign(x, centroids, x_sq, c_sq, out, hist, dtype, xsq_dtype, csq_dtype, B, N, K, D,
+                       x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2, workspace,
+                       wa, dev_status, stream);
+    if (st != FK_OK) return st;
+    return fk_centroid_accumulate(x, dtype, B, N, K, D, x_strides3, out, FK_I32, out_strides2,
+                                  hist, sums, counts, wu,
+                                  fk_centroid_accumulate_workspace_size(B, N, K), dev_status,
+                                  stream);
+  }
+  // fused path: same validation as fk_assign
+  if (!x || !centroids || !x_sq || !out || !x_strides3 || !c_strides3 || !xsq_strides2 ||
+      !out_strides2)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: null pointer argument");
+  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: c_sq without strides");
+  if (xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: x_sq dtype must be floating");
+  if (c_sq && csq_dtype != FK_F16 && csq_dtype != FK_BF16 && csq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: c_sq dtype must be floating");
+  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: K above 2^20");
+  if (N >= (1ll << 31) || B * ((N + kRows - 1) / kRows) >= (1ll << 31))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: problem too large");
+  const int64_t row_al = 8;
+  int64_t xs[3] = {x_strides3[0], x_strides3[1], x_strides3[2]};
+  int64_t cs[3] = {c_strides3[0], c_strides3[1], c_strides3[2]};
+  if (D == 1) { xs[2] = 1; cs[2] = 1; }
+  if (N == 1) xs[1] = (D + row_al - 1) / row_al * row_al;
+  if (K == 1) cs[1] = (D + row_al - 1) / row_al * row_al;
+  if (B == 1) { xs[0] = N * xs[1]; cs[0] = K * cs[1]; }
+  if (!fk_tma_compatible(x, dtype, D, xs))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: x rows not TMA-addressable");
+  if (!fk_tma_compatible(centroids, dtype, D, cs))
+    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: centroid rows not TMA-addressable");
+  if (dtype == FK_F16)
+    return assign_typed<__half>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N, K,
+                                D, xs, cs, xsq_strides2, csq_strides2, out_strides2, workspace,
+                                dev_status, s, sums);
+  return assign_typed<__nv_bfloat16>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B,
+                                     N, K, D, xs, cs, xsq_strides2, csq_strides2, out_strides2,
+                                     workspace, dev_status, s, sums);
 }
 
 // ---------------------------------------------------------------------------

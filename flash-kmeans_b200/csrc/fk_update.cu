@@ -10,7 +10,10 @@
 // accumulating in float32 registers and flushing one (vector) atomic per run
 // boundary.  The finalize kernel divides, keeps empty clusters, casts, and
 // also produces the next iteration's ||c||^2 and the centre shift.
+#include <type_traits>
+
 #include "fk_common.cuh"
+#include "fk_ptx.cuh"
 
 namespace fk {
 
@@ -91,128 +94,240 @@ __global__ void scatter_kernel(const I* __restrict__ ids, int64_t sib, int64_t s
   }
 }
 
-// 16-byte vector of T: raw load, then widen-and-add into float accumulators.
-template <typename T>
-struct Vec16 {
-  static constexpr int kElems = 16 / sizeof(T);
-  __device__ __forceinline__ static uint4 load(const T* p) {
-    return __ldg(reinterpret_cast<const uint4*>(p));
-  }
-  __device__ __forceinline__ static void add(float (&acc)[kElems], const uint4& u);
-};
-template <>
-__device__ __forceinline__ void Vec16<__half>::add(float (&acc)[8], const uint4& u) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-    acc[2 * i] += f.x;
-    acc[2 * i + 1] += f.y;
-  }
-}
-template <>
-__device__ __forceinline__ void Vec16<__nv_bfloat16>::add(float (&acc)[8], const uint4& u) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    acc[2 * i] += __uint_as_float(w[i] << 16);
-    acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-template <>
-__device__ __forceinline__ void Vec16<float>::add(float (&acc)[4], const uint4& u) {
-  acc[0] += __uint_as_float(u.x);
-  acc[1] += __uint_as_float(u.y);
-  acc[2] += __uint_as_float(u.z);
-  acc[3] += __uint_as_float(u.w);
-}
-
 constexpr int kSegWarps = 8;
-constexpr int kSegPos = 64;    // sorted positions per warp
-constexpr int kSegUnroll = 8;  // rows per lane group loaded before use
+constexpr int kSegPos = 64;  // sorted positions per warp (scalar fallback)
 
-template <int E>
-__device__ __forceinline__ void flush_run(float* dst, int d0, int D, bool vec, const float (&acc)[E]) {
-  if (vec && d0 + E <= D) {
-#pragma unroll
-    for (int i = 0; i < E; i += 4)
-      atomicAdd(reinterpret_cast<float4*>(dst + i),
-                make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
-  } else {
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (d0 + e < D) atomicAdd(dst + e, acc[e]);
-  }
-}
+// ---------------------------------------------------------------------------
+// Gathered segmented sums with bulk copies.  Block = 1 producer warp + 4
+// consumer warps and handles a contiguous range of sorted positions of one
+// batch and one column slice (grid (chunks, slices, B)).  The range is cut in
+// stages of R rows; consumer warp w owns a contiguous run of stages and two
+// private ring slots (double buffer).  The producer warp fetches the stage's
+// point indices (one per lane) and each lane issues one cp.async.bulk of its
+// row slice into the slot, completion counted in bytes on the slot's "full"
+// mbarrier -- hundreds of rows in flight per SM without register cost.  A
+// consumer sums runs of equal labels from shared memory (lane owns 4
+// consecutive columns of each 128-column sub-chunk) and flushes one vector
+// atomic per lane at each run boundary and at the end.
+// ---------------------------------------------------------------------------
+constexpr int kBulkConsumers = 4;
+constexpr int kBulkSlots = 2 * kBulkConsumers;
+constexpr int kBulkThreads = (1 + kBulkConsumers) * 32;
+constexpr int kBulkStageBytes = 8192;
 
-// grid (ceil(N / (8 warps * 64)), column slices, B).  A warp walks 64
-// consecutive sorted points.  Its lanes form 32/L groups of L lanes; a group
-// owns a contiguous share of the 64 points and reads each row slice as L
-// 16-byte vectors, so one load instruction fetches 32/L rows and
-// kSegUnroll instructions are in flight before any value is used.  Runs of
-// equal labels are summed in registers and flushed with vector atomics.
-// Rows must be 16-byte aligned; columns past D inside the last vector are
-// read (row padding) but never stored.
-template <typename T, int L>
-__global__ void __launch_bounds__(kSegWarps * 32)
-    segsum_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn,
-                  const int32_t* __restrict__ perm, const int32_t* __restrict__ sid,
-                  const int32_t* __restrict__ offs, const int32_t* __restrict__ hist, int N, int K,
-                  int D, float* __restrict__ sums, bool vflush) {
-  constexpr int E = Vec16<T>::kElems;
-  constexpr int G = 32 / L;          // row groups per warp
-  constexpr int PG = kSegPos / G;    // points per group
-  const int b = blockIdx.z;
+struct BulkParams {
+  int64_t sxb, sxn;          // element strides of x (batch, row); unit column stride
+  const int32_t* perm;       // (B, N) sorted point index
+  const int32_t* sid;        // (B, N) sorted label
+  const int32_t* offs;       // (B, K) exclusive scan of hist
+  const int32_t* hist;       // (B, K)
+  float* sums;               // (B, K, D)
+  int N, K, D;
+  int slice_elems;           // columns per slice (grid.y)
+  int slice_bytes;           // smem bytes reserved per row (multiple of 16)
+  int rows;                  // R rows per stage
+  int pos_per_block;
+  bool vflush;
+  int* status;
+};
+
+template <typename T, int NSUB>
+__global__ void __launch_bounds__(kBulkThreads)
+    segsum_bulk_kernel(const T* __restrict__ x, const BulkParams p) {
+  extern __shared__ __align__(128) uint8_t sm_raw[];
+  uint8_t* slots = sm_raw;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm_raw + kBulkSlots * kBulkStageBytes);
+  uint64_t* empty = full + kBulkSlots;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kBulkSlots);
+  constexpr int esz = sizeof(T);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t hb = static_cast<int64_t>(b) * K;
-  const int total_b = offs[hb + K - 1] + hist[hb + K - 1];
-  const int p0 = blockIdx.x * (kSegWarps * kSegPos) + warp * kSegPos;
-  if (p0 >= total_b) return;
-  const int np = min(kSegPos, total_b - p0);
-  const int64_t pb = static_cast<int64_t>(b) * N + p0;
-  int my_n0 = 0, my_n1 = 0, my_i0 = -1, my_i1 = -1;
-  if (lane < np) { my_n0 = __ldg(perm + pb + lane); my_i0 = __ldg(sid + pb + lane); }
-  if (lane + 32 < np) { my_n1 = __ldg(perm + pb + lane + 32); my_i1 = __ldg(sid + pb + lane + 32); }
-  const int g = lane / L;
-  const int d0 = blockIdx.y * (L * E) + (lane % L) * E;
-  const bool lane_active = d0 < D;
-  const int ng = max(0, min(PG, np - g * PG));  // points of this lane's group
-  const T* xb = x + b * sxb;
-  auto fetch = [&](int q, int a0, int a1) {  // value of position q from a per-lane pair
-    const int s0 = __shfl_sync(0xffffffffu, a0, q & 31);
-    const int s1 = __shfl_sync(0xffffffffu, a1, q & 31);
-    return (q >> 5) ? s1 : s0;
-  };
-  float acc[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  int cur = fetch(g * PG, my_i0, my_i1);
-  const int steps = min(PG, np);  // group 0 has the most points
-  for (int j0 = 0; j0 < steps; j0 += kSegUnroll) {
-    uint4 v[kSegUnroll];
-#pragma unroll
-    for (int u = 0; u < kSegUnroll; ++u) {
-      const int j = j0 + u;
-      const int n = fetch(g * PG + (j < PG ? j : 0), my_n0, my_n1);
-      v[u] = (j < ng && lane_active) ? Vec16<T>::load(xb + static_cast<int64_t>(n) * sxn + d0)
-                                     : make_uint4(0u, 0u, 0u, 0u);
+  const int b = blockIdx.z;
+  const int slice0 = blockIdx.y * p.slice_elems;
+  const int64_t hb = static_cast<int64_t>(b) * p.K;
+  const int total_b = p.offs[hb + p.K - 1] + p.hist[hb + p.K - 1];
+  const int P0 = blockIdx.x * p.pos_per_block;
+  const int P1 = min(P0 + p.pos_per_block, total_b);
+  if (P0 >= P1) return;  // whole block leaves before any barrier is used
+  const int R = p.rows;
+  const int nst = (P1 - P0 + R - 1) / R;
+  const int per = (nst + kBulkConsumers - 1) / kBulkConsumers;
+  // bytes actually copied per row: the slice, cut at the 16-byte-padded row end
+  const int rem = (p.D - slice0) * esz;
+  const int copy_bytes = min(p.slice_bytes, (rem + 15) & ~15);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBulkSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 32);
     }
-#pragma unroll
-    for (int u = 0; u < kSegUnroll; ++u) {
-      const int j = j0 + u;
-      const int id = fetch(g * PG + (j < PG ? j : 0), my_i0, my_i1);
-      if (j < ng) {
-        if (id != cur) {
-          if (lane_active) flush_run<E>(sums + (hb + cur) * D + d0, d0, D, vflush, acc);
-#pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = 0.f;
-          cur = id;
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int last_par[kBulkSlots];
+    for (int i = 0; i < kBulkSlots; ++i) last_par[i] = -1;
+    bool ok = true;
+    const T* xb = x + b * p.sxb + slice0;
+    const int32_t* pm = p.perm + static_cast<int64_t>(b) * p.N;
+    // Issue order: round r of every consumer, r = 0, 1, ...  The point indices
+    // of the next stage are loaded before waiting for the current slot.
+    const int nissue = per * kBulkConsumers;
+    auto stage_of = [&](int j, int& t, int& slot, uint32_t& ph) {
+      const int r = j / kBulkConsumers, w = j % kBulkConsumers;
+      t = w * per + r;
+      slot = 2 * w + (r & 1);
+      ph = static_cast<uint32_t>((r >> 1) & 1);
+      return t < min((w + 1) * per, nst);
+    };
+    auto load_idx = [&](int t, int& a, int& c) {
+      const int q0 = P0 + t * R;
+      const int nr = min(R, P1 - q0);
+      a = lane < nr ? __ldg(pm + q0 + lane) : 0;
+      c = lane + 32 < nr ? __ldg(pm + q0 + 32 + lane) : 0;
+    };
+    int na = 0, nc = 0, t_nx = 0, slot_nx = 0;
+    uint32_t ph_nx = 0;
+    int j = 0;
+    while (j < nissue && !stage_of(j, t_nx, slot_nx, ph_nx)) ++j;
+    if (j < nissue) load_idx(t_nx, na, nc);
+    while (ok && j < nissue) {
+      const int t = t_nx, slot = slot_nx;
+      const uint32_t ph = ph_nx;
+      const int ca = na, cc = nc;
+      int jn = j + 1;
+      while (jn < nissue && !stage_of(jn, t_nx, slot_nx, ph_nx)) ++jn;
+      if (jn < nissue) load_idx(t_nx, na, nc);  // in flight during the wait below
+      j = jn;
+      const bool got = mbar_wait(&empty[slot], ph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      const int q0 = P0 + t * R;
+      const int nr = min(R, P1 - q0);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nr * copy_bytes));
+      __syncwarp();
+      uint8_t* dst = slots + slot * kBulkStageBytes;
+      if (lane < nr)
+        bulk_load(dst + lane * p.slice_bytes, xb + static_cast<int64_t>(ca) * p.sxn,
+                  static_cast<uint32_t>(copy_bytes), &full[slot]);
+      if (lane + 32 < nr)
+        bulk_load(dst + (lane + 32) * p.slice_bytes, xb + static_cast<int64_t>(cc) * p.sxn,
+                  static_cast<uint32_t>(copy_bytes), &full[slot]);
+      if (lane == 0) last_par[slot] = static_cast<int>(ph);
+    }
+    if (!ok && lane == 0) {
+      for (int i = 0; i < kBulkSlots; ++i) {
+        if (last_par[i] < 0) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[i], static_cast<uint32_t>(last_par[i])) &&
+               globaltimer_ns() - t0 < 200000000ull) {
         }
-        Vec16<T>::add(acc, v[u]);
       }
     }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int w = warp - 1;
+    const int t_begin = w * per;
+    const int t_end = min(t_begin + per, nst);
+    float acc[NSUB][4];
+#pragma unroll
+    for (int s2 = 0; s2 < NSUB; ++s2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[s2][e] = 0.f;
+    int cur = -1;
+    auto flush = [&](int id) {
+#pragma unroll
+      for (int s2 = 0; s2 < NSUB; ++s2) {
+        const int col = slice0 + s2 * 128 + lane * 4;
+        float* dst = p.sums + (hb + id) * p.D + col;
+        if (col + 4 <= p.D && col - slice0 + 4 <= p.slice_elems && p.vflush) {
+          atomicAdd(reinterpret_cast<float4*>(dst),
+                    make_float4(acc[s2][0], acc[s2][1], acc[s2][2], acc[s2][3]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (col + e < p.D && col - slice0 + e < p.slice_elems) atomicAdd(dst + e, acc[s2][e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[s2][e] = 0.f;
+      }
+    };
+    const int32_t* sd = p.sid + static_cast<int64_t>(b) * p.N;
+    for (int t = t_begin, r = 0; t < t_end; ++t, ++r) {
+      const int slot = 2 * w + (r & 1);
+      const uint32_t ph = static_cast<uint32_t>((r >> 1) & 1);
+      const int q0 = P0 + t * R;
+      const int nr = min(R, P1 - q0);
+      const int id_lo = lane < nr ? __ldg(sd + q0 + lane) : -1;
+      const int id_hi = lane + 32 < nr ? __ldg(sd + q0 + 32 + lane) : -1;
+      const bool got = mbar_wait(&full[slot], ph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const uint8_t* base = slots + slot * kBulkStageBytes;
+      // add row i's slice (lane's 4 columns of each 128-column sub-chunk)
+      auto add_row = [&](float (&a)[NSUB][4], int i) {
+        const uint8_t* row = base + i * p.slice_bytes;
+#pragma unroll
+        for (int s2 = 0; s2 < NSUB; ++s2) {
+          const int off = (s2 * 128 + lane * 4) * esz;
+          if (off < p.slice_bytes) {
+            if constexpr (esz == 2) {
+              const uint2 u = *reinterpret_cast<const uint2*>(row + off);
+              if constexpr (std::is_same<T, __half>::value) {
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+                a[s2][0] += f0.x; a[s2][1] += f0.y; a[s2][2] += f1.x; a[s2][3] += f1.y;
+              } else {
+                a[s2][0] += __uint_as_float(u.x << 16); a[s2][1] += __uint_as_float(u.x & 0xFFFF0000u);
+                a[s2][2] += __uint_as_float(u.y << 16); a[s2][3] += __uint_as_float(u.y & 0xFFFF0000u);
+              }
+            } else {
+              const float4 u = *reinterpret_cast<const float4*>(row + off);
+              a[s2][0] += u.x; a[s2][1] += u.y; a[s2][2] += u.z; a[s2][3] += u.w;
+            }
+          }
+        }
+      };
+      auto id_at = [&](int i) {
+        return __shfl_sync(0xffffffffu, i < 32 ? id_lo : id_hi, i & 31);
+      };
+      int i = 0;
+      while (i < nr) {
+        const int id = id_at(i);
+        if (id != cur) {
+          if (cur >= 0) flush(cur);
+          cur = id;
+        }
+        // labels are sorted: rows i..i+7 share a label iff rows i and i+7 do.
+        // Then sum them with independent loads into a second accumulator.
+        if (i + 8 <= nr && id_at(i + 7) == id) {
+          float t8[NSUB][4];
+#pragma unroll
+          for (int s2 = 0; s2 < NSUB; ++s2)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) t8[s2][e] = 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            add_row(acc, i + u);
+            add_row(t8, i + u + 1);
+          }
+#pragma unroll
+          for (int s2 = 0; s2 < NSUB; ++s2)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[s2][e] += t8[s2][e];
+          i += 8;
+        } else {
+          add_row(acc, i);
+          i += 1;
+        }
+      }
+      mbar_arrive(&empty[slot]);
+    }
+    if (cur >= 0) flush(cur);
   }
-  if (ng > 0 && lane_active) flush_run<E>(sums + (hb + cur) * D + d0, d0, D, vflush, acc);
 }
 
 // Fallback for rows that are not 16-byte aligned: one warp per 64 points,
@@ -248,33 +363,66 @@ __global__ void __launch_bounds__(kSegWarps * 32)
   }
 }
 
-// One warp per (b, k): reference finalize (centroid_update_triton.py:378-385,
-// torch_fallback.py:101-108) plus ||c_new||^2 and the shift.  Lane l owns
-// columns 4l..4l+3 of every 128-column slice (float4 loads of the sums).
+// Four consecutive elements of T as one vector load / store.
 template <typename T>
-__device__ __forceinline__ void fin_elem(float sumv, int32_t cnt, float fc, T ov, T* dst,
-                                         float& ss, float& cs) {
-  const T nv = cnt > 0 ? Elem<T>::from_f(sumv / fc) : ov;
-  *dst = nv;
-  const float nf = Elem<T>::to_f(nv);
-  const float df = Elem<T>::round(nf - Elem<T>::to_f(ov));
-  ss += df * df;
-  cs += Elem<T>::round(nf * nf);
-}
+struct Quad;
+template <>
+struct Quad<__half> {
+  __device__ __forceinline__ static void load(const __half* p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    f[0] = a.x; f[1] = a.y; f[2] = c.x; f[3] = c.y;
+  }
+  __device__ __forceinline__ static void store(__half* p, const float (&f)[4]) {
+    const __half2 a = __floats2half2_rn(f[0], f[1]), c = __floats2half2_rn(f[2], f[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&c);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+};
+template <>
+struct Quad<__nv_bfloat16> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    f[0] = __uint_as_float(u.x << 16); f[1] = __uint_as_float(u.x & 0xFFFF0000u);
+    f[2] = __uint_as_float(u.y << 16); f[3] = __uint_as_float(u.y & 0xFFFF0000u);
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float (&f)[4]) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), c = __floats2bfloat162_rn(f[2], f[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&c);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+};
+template <>
+struct Quad<float> {
+  __device__ __forceinline__ static void load(const float* p, float (&f)[4]) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float (&f)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+};
 
+// One warp per (b, k) row: the reference finalize (centroid_update_triton.py:378-385,
+// torch_fallback.py:101-108) -- new = cnt ? sums / cnt : old, cast -- plus the
+// next ||c||^2 with the reference's rounding, the row's shift
+// round(||round(new - old)||), and optionally zeroing sums/counts for the next
+// iteration.  Vector path: lane owns 4 consecutive columns per 128.
 template <typename T>
 __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ counts,
                                 const T* __restrict__ old, int64_t sob, int64_t sok, int64_t sod,
                                 T* __restrict__ out, int64_t snb, int64_t snk, int64_t snd, int B,
                                 int K, int D, float* __restrict__ csq_out,
-                                float* __restrict__ shift_out, bool reset) {
-  const int wpb = blockDim.x >> 5;
+                                float* __restrict__ shift_out, bool reset, bool vec) {
   const int lane = threadIdx.x & 31;
-  const int64_t rows = static_cast<int64_t>(B) * K;
-  const bool vec = (D % 4 == 0) && sod == 1 && snd == 1;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   float wmax = 0.f;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); r < rows;
-       r += static_cast<int64_t>(gridDim.x) * wpb) {
+  if (r < static_cast<int64_t>(B) * K) {
     const int64_t b = r / K, k = r % K;
     const int32_t cnt = counts[r];
     const float fc = static_cast<float>(cnt);
@@ -284,25 +432,37 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
     float ss = 0.f, cs = 0.f;
     if (vec) {
       for (int d = lane * 4; d < D; d += 128) {
-        const float4 sv = *reinterpret_cast<const float4*>(s + d);
+        float sv[4], ov[4], nv[4];
+        Quad<float>::load(s + d, sv);
+        Quad<T>::load(o + d, ov);
         if (reset) *reinterpret_cast<float4*>(s + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-        const float svs[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) fin_elem<T>(svs[e], cnt, fc, o[d + e], nw + d + e, ss, cs);
+        for (int e = 0; e < 4; ++e) {
+          nv[e] = cnt > 0 ? Elem<T>::round(sv[e] / fc) : ov[e];
+          const float df = Elem<T>::round(nv[e] - ov[e]);
+          ss += df * df;
+          cs += Elem<T>::round(nv[e] * nv[e]);
+        }
+        Quad<T>::store(nw + d, nv);
       }
     } else {
       for (int d = lane; d < D; d += 32) {
         const float sv = s[d];
         if (reset) s[d] = 0.f;
-        fin_elem<T>(sv, cnt, fc, o[d * sod], nw + d * snd, ss, cs);
+        const float ov = Elem<T>::to_f(o[d * sod]);
+        const float nv = cnt > 0 ? Elem<T>::round(sv / fc) : ov;
+        nw[d * snd] = Elem<T>::from_f(nv);
+        const float df = Elem<T>::round(nv - ov);
+        ss += df * df;
+        cs += Elem<T>::round(nv * nv);
       }
     }
     ss = warp_sum(ss);
     cs = warp_sum(cs);
-    if (reset && lane == 0) counts[r] = 0;
     if (lane == 0) {
+      if (reset) counts[r] = 0;
       if (csq_out) csq_out[r] = Elem<T>::round(cs);
-      wmax = fmaxf(wmax, Elem<T>::round(sqrtf(ss)));
+      wmax = Elem<T>::round(sqrtf(ss));
     }
   }
   // one atomic per block for the shift (non-negative floats order as uints)
@@ -311,7 +471,7 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
   __syncthreads();
   if (threadIdx.x == 0 && shift_out) {
     float m = 0.f;
-    for (int w = 0; w < wpb; ++w) m = fmaxf(m, blk_max[w]);
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, blk_max[w]);
     atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(m));
   }
 }
@@ -345,36 +505,78 @@ static int hist_scatter(const void* ids, const int64_t* is, int64_t B, int64_t N
   return check_launch("scatter_kernel");
 }
 
-template <typename T, int L>
-static void launch_segsum(const T* x, const int64_t* xs, int64_t B, int64_t N, int64_t K, int64_t D,
-                          const int32_t* perm, const int32_t* sid, const int32_t* offs,
-                          const int32_t* hist, float* sums, bool vflush, cudaStream_t s) {
-  constexpr int E = 16 / sizeof(T);
-  dim3 grid(static_cast<unsigned>((N + kSegWarps * kSegPos - 1) / (kSegWarps * kSegPos)),
-            static_cast<unsigned>((D + L * E - 1) / (L * E)), static_cast<unsigned>(B));
-  segsum_kernel<T, L><<<grid, kSegWarps * 32, 0, s>>>(x, xs[0], xs[1], perm, sid, offs, hist,
-                                                      (int)N, (int)K, (int)D, sums, vflush);
+template <typename T>
+static int bulk_smem_attr(int nsub, int smem) {
+  static bool done[4][64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device");
+  if (done[nsub - 1][dev]) return FK_OK;
+  cudaError_t e;
+  switch (nsub) {
+    case 1: e = cudaFuncSetAttribute(segsum_bulk_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 2: e = cudaFuncSetAttribute(segsum_bulk_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 3: e = cudaFuncSetAttribute(segsum_bulk_kernel<T, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    default: e = cudaFuncSetAttribute(segsum_bulk_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+  }
+  if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute(segsum): %s", cudaGetErrorString(e));
+  done[nsub - 1][dev] = true;
+  return FK_OK;
 }
 
 template <typename T>
 static int segsum_typed(const void* x, const int64_t* xs, int64_t B, int64_t N, int64_t K,
                         int64_t D, const int32_t* perm, const int32_t* sid, const int32_t* offs,
-                        const int32_t* hist, float* sums, cudaStream_t s) {
+                        const int32_t* hist, float* sums, int* status, cudaStream_t s) {
   constexpr int E = 16 / sizeof(T);
-  const bool vload = xs[2] == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                     ((xs[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0) &&
-                     ((xs[0] * static_cast<int64_t>(sizeof(T))) % 16 == 0 || B == 1) &&
-                     xs[1] >= (D + E - 1) / E * E;
+  const bool aligned = xs[2] == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       ((xs[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0) &&
+                       ((xs[0] * static_cast<int64_t>(sizeof(T))) % 16 == 0 || B == 1) &&
+                       xs[1] >= (D + E - 1) / E * E;
   const bool vflush = (D % 4 == 0) && (reinterpret_cast<uintptr_t>(sums) % 16 == 0);
   const T* xt = static_cast<const T*>(x);
-  if (vload) {
-    const int64_t vecs = (D + E - 1) / E;  // 16-byte vectors per row
-    if (vecs <= 8)
-      launch_segsum<T, 8>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
-    else if (vecs <= 16)
-      launch_segsum<T, 16>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
-    else
-      launch_segsum<T, 32>(xt, xs, B, N, K, D, perm, sid, offs, hist, sums, vflush, s);
+  if (aligned) {
+    // column slice: up to 512 columns and 1024 bytes, a multiple of 128 columns
+    const int max_cols = (1024 / static_cast<int>(sizeof(T))) >= 512 ? 512 : 1024 / static_cast<int>(sizeof(T));
+    const int64_t Dpad = (D + E - 1) / E * E;
+    int slice = static_cast<int>(Dpad < max_cols ? Dpad : max_cols);
+    const int nsub = (slice + 127) / 128;
+    slice = slice < nsub * 128 ? slice : nsub * 128;
+    const int slice_bytes = (slice * static_cast<int>(sizeof(T)) + 15) & ~15;
+    BulkParams bp;
+    bp.sxb = xs[0];
+    bp.sxn = xs[1];
+    bp.perm = perm;
+    bp.sid = sid;
+    bp.offs = offs;
+    bp.hist = hist;
+    bp.sums = sums;
+    bp.N = static_cast<int>(N);
+    bp.K = static_cast<int>(K);
+    bp.D = static_cast<int>(D);
+    bp.slice_elems = slice;
+    bp.slice_bytes = slice_bytes;
+    bp.rows = kBulkStageBytes / slice_bytes < 64 ? kBulkStageBytes / slice_bytes : 64;
+    const int nslices = static_cast<int>((D + slice - 1) / slice);
+    const int sms = sm_count_current() > 0 ? sm_count_current() : 148;
+    const int64_t unit = static_cast<int64_t>(bp.rows) * kBulkConsumers;
+    int64_t target_blocks = static_cast<int64_t>(sms) * 9;  // ~3 waves of 3 blocks per SM
+    int64_t ppb = (N * B * nslices + target_blocks - 1) / target_blocks;
+    ppb = (ppb + unit - 1) / unit * unit;
+    if (ppb < unit) ppb = unit;
+    bp.pos_per_block = static_cast<int>(ppb);
+    bp.vflush = vflush;
+    bp.status = status;
+    const size_t smem = kBulkSlots * kBulkStageBytes + 2 * kBulkSlots * 8 + 16;
+    int st = bulk_smem_attr<T>(nsub, static_cast<int>(smem));
+    if (st != FK_OK) return st;
+    dim3 grid(static_cast<unsigned>((N + ppb - 1) / ppb), static_cast<unsigned>(nslices),
+              static_cast<unsigned>(B));
+    switch (nsub) {
+      case 1: segsum_bulk_kernel<T, 1><<<grid, kBulkThreads, smem, s>>>(xt, bp); break;
+      case 2: segsum_bulk_kernel<T, 2><<<grid, kBulkThreads, smem, s>>>(xt, bp); break;
+      case 3: segsum_bulk_kernel<T, 3><<<grid, kBulkThreads, smem, s>>>(xt, bp); break;
+      default: segsum_bulk_kernel<T, 4><<<grid, kBulkThreads, smem, s>>>(xt, bp); break;
+    }
   } else {
     dim3 grid(static_cast<unsigned>((N + kSegWarps * kSegPos - 1) / (kSegWarps * kSegPos)),
               static_cast<unsigned>(D > 32 * 16 ? 16 : (D + 31) / 32), static_cast<unsigned>(B));
@@ -438,11 +640,11 @@ extern "C" int fk_centroid_accumulate(const void* x, int dtype, int64_t B, int64
   if (st) return st;
   switch (dtype) {
     case FK_F16:
-      return segsum_typed<__half>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, s);
+      return segsum_typed<__half>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, dev_status, s);
     case FK_BF16:
-      return segsum_typed<__nv_bfloat16>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, s);
+      return segsum_typed<__nv_bfloat16>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, dev_status, s);
     case FK_F32:
-      return segsum_typed<float>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, s);
+      return segsum_typed<float>(x, x_strides3, B, N, K, D, perm, sid, offs, h, sums, dev_status, s);
     default:
       return fail(FK_ERR_INVALID_ARG, "fk_centroid_accumulate: unsupported dtype %d", dtype);
   }
@@ -465,27 +667,33 @@ extern "C" int fk_centroid_finalize(float* sums, int32_t* counts, const void* ol
   }
   if (B == 0) return FK_OK;
   const int64_t rows = B * K;
-  const int grid = grid_for(rows, 8, 16);
+  const int grid = static_cast<int>((rows + 7) / 8);  // one warp per row
   const int64_t* os = old_strides3;
   const int64_t* ns = new_strides3;
+  const int64_t eb = dtype_bytes(dtype);
+  const bool vec = D % 4 == 0 && os[2] == 1 && ns[2] == 1 && os[1] % 4 == 0 && ns[1] % 4 == 0 &&
+                   (os[0] % 4 == 0 || B == 1) && (ns[0] % 4 == 0 || B == 1) &&
+                   reinterpret_cast<uintptr_t>(old_centroids) % (4 * eb) == 0 &&
+                   reinterpret_cast<uintptr_t>(new_centroids) % (4 * eb) == 0 &&
+                   reinterpret_cast<uintptr_t>(sums) % 16 == 0;
   switch (dtype) {
     case FK_F16:
       finalize_kernel<__half><<<grid, 256, 0, s>>>(
           sums, counts, static_cast<const __half*>(old_centroids), os[0], os[1], os[2],
           static_cast<__half*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D, csq_out,
-          shift_out, reset_accumulators != 0);
+          shift_out, reset_accumulators != 0, vec);
       break;
     case FK_BF16:
       finalize_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
           sums, counts, static_cast<const __nv_bfloat16*>(old_centroids), os[0], os[1], os[2],
           static_cast<__nv_bfloat16*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D,
-          csq_out, shift_out, reset_accumulators != 0);
+          csq_out, shift_out, reset_accumulators != 0, vec);
       break;
     case FK_F32:
       finalize_kernel<float><<<grid, 256, 0, s>>>(
           sums, counts, static_cast<const float*>(old_centroids), os[0], os[1], os[2],
           static_cast<float*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D, csq_out,
-          shift_out, reset_accumulators != 0);
+          shift_out, reset_accumulators != 0, vec);
       break;
     default:
       return fail(FK_ERR_INVALID_ARG, "fk_centroid_finalize: unsupported dtype %d", dtype);

@@ -46,6 +46,9 @@ SIGNATURES = {
     "fk_assign_workspace_size": (_S, [_L, _L, _I]),
     "fk_assign": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL, _PL, _PL,
                        _PL, _P, _S, _P, _P]),
+    "fk_assign_accumulate_workspace_size": (_S, [_L, _L, _L, _L, _I]),
+    "fk_assign_accumulate": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL,
+                                  _PL, _PL, _PL, _P, _S, _P, _P]),
     "fk_assign_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL,
                                       _PL, _PL, _PL, _PL, _P, _P]),
     "fk_centroid_accumulate_workspace_size": (_S, [_L, _L, _L]),

@@ -15,8 +15,8 @@ B200 design:
   copy of block i+1 (and of the next iteration's first blocks) overlaps the
   assignment of block i, ordered by events only (no host waits);
 * x_sq per block is computed once and kept on the device;
-* the assignment kernel also produces the block's histogram, which the
-  accumulate step reuses (no separate histogram pass);
+* each block goes through fk_assign_accumulate: labels, counts and per-cluster
+  row sums in one call (one kernel for 16-bit data with D <= 128);
 * reduction: every device ends with identical sums/counts after an NCCL
   all-reduce (single-process communicator over the devices, or the process
   group when one process drives one GPU), then finalizes its own replica, so
@@ -89,10 +89,9 @@ class _DeviceLane:
             self.stat = torch.zeros(4, dtype=torch.int32, device=dev)
             self.csq_valid = False
             lib = nat.load()
-            self.ws_a = torch.empty(lib.fk_assign_workspace_size(1, K, nat.dtype_code(dtype)),
-                                    dtype=torch.uint8, device=dev)
-            self.ws_u = torch.empty(lib.fk_centroid_accumulate_workspace_size(1, nb, K),
-                                    dtype=torch.uint8, device=dev)
+            self.ws = torch.empty(
+                lib.fk_assign_accumulate_workspace_size(1, nb, K, D, nat.dtype_code(dtype)),
+                dtype=torch.uint8, device=dev)
         # Copies form one sequence over passes: element s streams block s % nb
         # into buffer slot s % 2, so consecutive copies always alternate slots.
         self._issued = 0
@@ -156,21 +155,17 @@ class _DeviceLane:
                 lo, hi = n0 - self.p0, n1 - self.p0
                 out = self.labels[:, lo:hi]
                 c_sq = self.csq if self.csq_valid else None
-                if not assign_only:
-                    self.hist.zero_()
-                nat.check(lib.fk_assign(
-                    nat.ptr(xb), nat.ptr(self.c_cur), nat.ptr(xsq), nat.ptr(c_sq), nat.ptr(out),
-                    None if assign_only else nat.ptr(self.hist), nat.dtype_code(xb.dtype),
-                    nat.dtype_code(xsq.dtype), nat.FK_F32, 1, nb, K, D, nat.strides(xb, 3),
-                    nat.strides(self.c_cur, 3), nat.strides(xsq, 2), nat.strides(self.csq, 2),
-                    nat.strides(out, 2), nat.ptr(self.ws_a), self.ws_a.numel(), status, s),
-                    "fk_assign")
-                if not assign_only:
-                    nat.check(lib.fk_centroid_accumulate(
-                        nat.ptr(xb), nat.dtype_code(xb.dtype), 1, nb, K, D, nat.strides(xb, 3),
-                        nat.ptr(out), nat.FK_I32, nat.strides(out, 2), nat.ptr(self.hist),
-                        nat.ptr(self.sums), nat.ptr(self.cnt), nat.ptr(self.ws_u),
-                        self.ws_u.numel(), status, s), "fk_centroid_accumulate")
+                args = (nat.ptr(xb), nat.ptr(self.c_cur), nat.ptr(xsq), nat.ptr(c_sq), nat.ptr(out))
+                tail = (nat.dtype_code(xsq.dtype), nat.FK_F32, 1, nb, K, D, nat.strides(xb, 3),
+                        nat.strides(self.c_cur, 3), nat.strides(xsq, 2), nat.strides(self.csq, 2),
+                        nat.strides(out, 2), nat.ptr(self.ws), self.ws.numel(), status, s)
+                if assign_only:
+                    nat.check(lib.fk_assign(*args, None, nat.dtype_code(xb.dtype), *tail),
+                              "fk_assign")
+                else:  # labels, counts and row sums of this block in one pass
+                    nat.check(lib.fk_assign_accumulate(*args, nat.ptr(self.cnt), nat.ptr(self.sums),
+                                                       nat.dtype_code(xb.dtype), *tail),
+                              "fk_assign_accumulate")
                 self.free[slot].record(ks)
                 self._refill(wrap)
             self._pass += 1

@@ -7,10 +7,10 @@ assignment + update + shift per iteration, ``break`` when the shift drops
 below ``tol`` (returning the centroids that produced the last labels), and the
 result ``(cluster_ids int32 (B,N), centroids (B,K,D) x.dtype, n_iters)``.
 
-Per iteration the B200 build launches: fk_assign (labels + fused histogram),
-fk_centroid_accumulate (scan, scatter, segmented sums) and fk_centroid_finalize
-(means, next ||c||^2, shift, and zeroing of the accumulators for the next
-iteration) -- six kernels, no memsets.  The host reads the 8-byte
+Per iteration the B200 build launches fk_assign_accumulate (labels, and the
+points' rows and counts added to the per-cluster sums in the same pass over x)
+and fk_centroid_finalize (means, next ||c||^2, shift, and zeroing of the
+accumulators for the next iteration) -- no memsets, x read once.  The host reads the 8-byte
 (shift, status) record only when ``tol > 0`` or ``verbose`` needs it; with
 ``tol <= 0`` the shift can never be below tol, so iterations are queued back
 to back with no host synchronisation.
@@ -51,10 +51,9 @@ class LloydEngine:
         self.stat_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
         self.csq_valid = False
         lib = nat.load()
-        self.ws_a = torch.empty(lib.fk_assign_workspace_size(B, K, nat.dtype_code(dtype)),
-                                dtype=torch.uint8, device=dev)
-        self.ws_u = torch.empty(lib.fk_centroid_accumulate_workspace_size(B, N, K),
-                                dtype=torch.uint8, device=dev)
+        self.ws = torch.empty(
+            lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype)),
+            dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None
 
@@ -73,7 +72,7 @@ class LloydEngine:
         """One Lloyd iteration: ids <- assign(centroids); c_nxt <- update; shift.
 
         ``ev_assign``: optional (start, end) CUDA events recorded around the
-        assignment on the current stream (used by the benchmark)."""
+        assignment (with its fused accumulation) on the current stream."""
         lib = nat.load()
         B, N, K, D = self.B, self.N, self.K, self.D
         x, dev = self.x, self.device
@@ -82,19 +81,15 @@ class LloydEngine:
         c_sq = self.csq if self.csq_valid else None
         if ev_assign is not None:
             ev_assign[0].record()
-        nat.check(lib.fk_assign(
+        nat.check(lib.fk_assign_accumulate(
             nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.x_sq), nat.ptr(c_sq), nat.ptr(self.ids),
-            nat.ptr(self.hist), nat.dtype_code(x.dtype), nat.dtype_code(self.x_sq.dtype),
-            nat.FK_F32, B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
-            nat.strides(self.x_sq, 2), nat.strides(self.csq, 2), nat.strides(self.ids, 2),
-            nat.ptr(self.ws_a), self.ws_a.numel(), status, s), "fk_assign")
+            nat.ptr(self.hist), nat.ptr(self.sums), nat.dtype_code(x.dtype),
+            nat.dtype_code(self.x_sq.dtype), nat.FK_F32, B, N, K, D, nat.strides(x, 3),
+            nat.strides(self.c_cur, 3), nat.strides(self.x_sq, 2), nat.strides(self.csq, 2),
+            nat.strides(self.ids, 2), nat.ptr(self.ws), self.ws.numel(), status, s),
+            "fk_assign_accumulate")
         if ev_assign is not None:
             ev_assign[1].record()
-        nat.check(lib.fk_centroid_accumulate(
-            nat.ptr(x), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.ptr(self.ids),
-            nat.FK_I32, nat.strides(self.ids, 2), nat.ptr(self.hist), nat.ptr(self.sums),
-            nat.ptr(self.hist), nat.ptr(self.ws_u), self.ws_u.numel(), status, s),
-            "fk_centroid_accumulate")
         nat.check(lib.fk_centroid_finalize(
             nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
             nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),

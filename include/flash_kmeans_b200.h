@@ -105,6 +105,23 @@ int fk_assign(const void* x, const void* centroids, const void* x_sq, const void
               const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
               size_t workspace_bytes, int32_t* dev_status, void* stream);
 
+/* Assignment fused with the centroid accumulation of one Lloyd iteration
+ * (replaces the pair euclid_assign_triton + triton_centroid_update_sorted_euclid
+ * in _euclid_iter, flash_kmeans/kmeans_triton_impl.py:11-17, up to the
+ * finalize).  Same arguments as fk_assign plus `sums` (B,K,D float32
+ * contiguous); `counts` (B,K int32) is required.  Labels are written to `out`,
+ * their histogram is ADDED to `counts` and the rows of x are ADDED to
+ * sums[label].  With 16-bit x and D <= 128 this is one kernel that reads x
+ * once; otherwise it runs fk_assign then fk_centroid_accumulate. */
+size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
+int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
+                         int32_t* out, int32_t* counts, float* sums, int dtype, int xsq_dtype,
+                         int csq_dtype, int64_t B, int64_t N, int64_t K, int64_t D,
+                         const int64_t* x_strides3, const int64_t* c_strides3,
+                         const int64_t* xsq_strides2, const int64_t* csq_strides2,
+                         const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
+                         int32_t* dev_status, void* stream);
+
 /* fk_assign for callers that cannot allocate (no counterpart in the reference).
  * Some hosts give a plugin only its inputs and outputs: a serving framework's
  * custom-op interface without a workspace hook, a memory pool that forbids side

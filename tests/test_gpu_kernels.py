@@ -191,3 +191,39 @@ def test_update_bad_label_reports_device_status(fk):
         DeviceStatus.raise_if_set(x.device)
     DeviceStatus.raise_if_set(x.device)  # cleared
     assert int(cnt.sum()) == 63
+
+
+# -------------------------------------------------- fused assign + accumulate
+@pytest.mark.parametrize("dt,B,N,K,D", [
+    ("float16", 3, 5000, 1000, 128), ("float16", 2, 700, 70, 64), ("bfloat16", 2, 900, 33, 100),
+    ("float16", 1, 1000, 50, 17), ("float16", 1, 640, 40, 192), ("float32", 2, 800, 60, 48)])
+def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
+    """fk_assign_accumulate (fused for 16-bit D<=128, internal fallback otherwise) equals
+    fk_assign + fk_centroid_accumulate: labels bit-identical, counts exact, sums to fp32 order."""
+    from flash_kmeans import _native as nat
+    from flash_kmeans import _ops
+    lib = nat.load()
+    rng = np.random.default_rng(B * 7 + D)
+    x = _ops.ensure_tma(_dev(ko.round_to(rng.standard_normal((B, N, D), dtype=np.float32), dt), dt))
+    c = _ops.ensure_tma(_dev(ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt), dt))
+    xsq = _ops.row_sqnorm(x)
+    ref = _ops.assign(x, c, xsq)
+    ref_s = torch.zeros((B, K, D), device="cuda")
+    ref_c = torch.zeros((B, K), dtype=torch.int32, device="cuda")
+    _ops.accumulate(x, ref, ref_s, ref_c)
+    out = torch.full((B, N), -1, dtype=torch.int32, device="cuda")
+    sums = torch.zeros((B, K, D), device="cuda")
+    cnts = torch.zeros((B, K), dtype=torch.int32, device="cuda")
+    ws = torch.empty(lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(x.dtype)),
+                     dtype=torch.uint8, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    nat.check(lib.fk_assign_accumulate(
+        nat.ptr(x), nat.ptr(c), nat.ptr(xsq), None, nat.ptr(out), nat.ptr(cnts), nat.ptr(sums),
+        nat.dtype_code(x.dtype), nat.dtype_code(xsq.dtype), 0, B, N, K, D, nat.strides(x, 3),
+        nat.strides(c, 3), nat.strides(xsq, 2), None, nat.strides(out, 2), nat.ptr(ws), ws.numel(),
+        nat.ptr(status), nat.stream_handle(x.device)), "fk_assign_accumulate")
+    torch.cuda.synchronize()
+    assert int(status[0]) == 0
+    assert torch.equal(out, ref)
+    assert torch.equal(cnts, ref_c)
+    torch.testing.assert_close(sums, ref_s, rtol=1e-5, atol=1e-3)
