@@ -1,7 +1,8 @@
 // Nearest-centroid assignment on sm_100a (replaces _euclid_assign_kernel and
 // _euclid_assign_kernel_split_d, flash_kmeans/assign_euclid_triton.py:804-1030).
 //
-// One persistent CTA per SM walks (batch, 128-point tile) work items.  Per
+// One persistent CTA per SM walks a contiguous range of (batch, 128-point tile)
+// work items.  Per
 // item it streams the batch's centroids in tiles of 256 through a TMA ring and
 // computes the 128 x 256 cross products x.c^T with tcgen05.mma into one of
 // two TMEM accumulators (2 x 256 of the 512 columns), so the epilogue of tile
@@ -12,8 +13,10 @@
 // +1 on that label's count).
 //
 // Roles (warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
-// 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4).. and half (w-2)/4 of
-// each 256-column tile), 10..13 = f32 split converters (3xTF32 mode only).
+// 2..(2+EPI-1) = epilogue (warp w reads TMEM lanes 32*(w%4).. and column
+// group (w-2)/4 of each 256-column tile; EPI = 16 for 16-bit inputs, 8 for
+// float32), then 4 more warps: f32 split converters (3xTF32 mode) or sum
+// warps (fused accumulation).
 //
 // Modes:
 //   0  16-bit x with x_sq in the same dtype: dist = r(r(x_sq - 2 r(x.c)) + c_sq),
@@ -23,7 +26,7 @@
 //   1  16-bit x, float32 x_sq: cross rounded to the 16-bit dtype (the bmm output
 //      dtype), then the float32 chain (type promotion of torch_fallback.py:41-45).
 //   2  float32 x: cross = 3xTF32 (hi*hi + hi*lo + lo*hi, hi = tf32-rounded
-//      value, lo = exact remainder, split in shared memory by warps 10..13),
+//      value, lo = exact remainder, split in shared memory by the 4 extra warps),
 //      float32 chain.
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
@@ -38,17 +41,17 @@ namespace fk {
 
 constexpr int kRows = 128;            // points per tile (MMA M)
 constexpr int kCent = 256;            // centroids per tile (MMA N)
+constexpr int kAcc = 2;               // TMEM accumulators (kAcc x kCent = all 512 columns)
 constexpr int kChunkB = 128;          // bytes per row chunk = one 128B swizzle span
 constexpr int kXChunk = kRows * kChunkB;   // 16 KB
 constexpr int kCChunk = kCent * kChunkB;   // 32 KB
-constexpr int kEpiWarps = 8;
-constexpr int kEpiWarp0 = 2;
-constexpr int kConvWarp0 = 10;
-constexpr int kConvWarps = 4;
+constexpr int kEpiWarp0 = 2;           // epilogue warps start here (EPI of them)
+constexpr int kConvWarps = 4;          // fp32 split warps / sum warps after the epilogue
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
 
-template <int MODE, bool XRES, int STAGES, bool FUSE = false>
+template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8>
 struct Layout {
+  static constexpr int kGroups = EPI / 4;  // column groups of each 256-centroid tile
   static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
   static constexpr int XB = FUSE ? 3 : 2;              // resident x tile buffers
   static constexpr int x_off = 0;
@@ -60,16 +63,22 @@ struct Layout {
   static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
   static constexpr int merge_off = stages_off + STAGES * stage_bytes;
-  static constexpr int merge_bytes = 2 * kRows * 8;     // [parity][row] (value, index)
+  // [parity][group 1..G-1][row] (value, index) candidates for the merge
+  static constexpr int merge_bytes = 2 * (kGroups - 1) * kRows * 8;
   static constexpr int lab_off = merge_off + merge_bytes;
   static constexpr int lab_bytes = FUSE ? 2 * kRows * 4 : 0;  // [parity][row] label or -1
-  static constexpr int bar_off = lab_off + lab_bytes;
-  // x_full[3] x_empty[3] c_full[S] c_empty[S] conv_full[S] acc_full[2] acc_empty[2]
+  // mode 0: each epilogue thread's saved chunk of 16 packed distances, as
+  // [unit 0..3][epilogue thread] 16-byte units (conflict-free stores)
+  static constexpr int save_stride = EPI * 32;  // in 16-byte units
+  static constexpr int save_off = lab_off + lab_bytes;
+  static constexpr int save_bytes = (MODE == 0) ? 4 * save_stride * 16 : 0;
+  static constexpr int bar_off = save_off + save_bytes;
+  // x_full[3] x_empty[3] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
-  static constexpr int nbars = 6 + 3 * STAGES + 4 + 4 + 4 + 1;
+  static constexpr int nbars = 6 + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
-  static constexpr int threads = ((MODE == 2 || FUSE) ? 14 : 10) * 32;
+  static constexpr int threads = (kEpiWarp0 + EPI + ((MODE == 2 || FUSE) ? kConvWarps : 0)) * 32;
 };
 
 struct AssignParams {
@@ -239,6 +248,76 @@ struct ArgminPacked {  // mode 0: two columns per 32-bit register
   }
 };
 
+// Running argmin for mode 0 that spends about one ALU operation per column
+// pair: each 32-column chunk is reduced to its minimum with a tree of packed
+// min operations and compared once with the running best.  When a thread's
+// chunk minimum is strictly below its best, the thread stores the chunk's 16
+// packed distances in its own shared-memory slot (predicated stores on the
+// otherwise idle load/store pipe).  The saved chunk is then the first chunk
+// holding the final minimum (later chunks that only tie are not saved), so
+// the first column equal to the minimum inside it is the lowest-index
+// argmin.  result() finds that column once per tile.
+template <typename T>
+struct ArgminSaved {
+  uint32_t best2;  // running minimum, in both halves
+  int chunk;       // col >> 5 of the saved chunk, -1 while nothing is saved
+  uint4* slot;     // this thread's four 16-byte units, `stride` units apart
+  int stride;
+  __device__ __forceinline__ void init(uint4* s, int st) {
+    best2 = Pack2<T>::kInf2;
+    chunk = -1;
+    slot = s;
+    stride = st;
+  }
+  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint32_t* cw,
+                                          uint32_t xsq2, int col0) {
+    uint32_t d[16];
+#pragma unroll
+    for (int pp = 0; pp < 16; ++pp)
+      d[pp] = Pack2<T>::dist(__uint_as_float(v[2 * pp]), __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
+    uint32_t m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = Pack2<T>::min2(d[i], d[i + 8]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = Pack2<T>::min2(m[i], m[i + 4]);
+    m[0] = Pack2<T>::min2(m[0], m[2]);
+    m[1] = Pack2<T>::min2(m[1], m[3]);
+    m[0] = Pack2<T>::min2(m[0], m[1]);
+    const uint32_t mm = Pack2<T>::min2(m[0], __byte_perm(m[0], 0, 0x1032));  // both halves
+    if (Pack2<T>::lt_mask(mm, best2) != 0u) {
+      best2 = mm;
+      chunk = col0 >> 5;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        slot[u * stride] = make_uint4(d[4 * u], d[4 * u + 1], d[4 * u + 2], d[4 * u + 3]);
+    }
+  }
+  // first_col: the lowest column this thread visits (the answer when every
+  // distance it saw was +inf, matching argmin's first index)
+  __device__ __forceinline__ void result(float& val, int& idx, int first_col) const {
+    val = __int_as_float(0x7f800000);
+    idx = first_col;
+    if (chunk < 0) return;
+    val = Pack2<T>::lo(best2);
+    uint32_t w[16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint4 q = slot[u * stride];
+      w[4 * u] = q.x;
+      w[4 * u + 1] = q.y;
+      w[4 * u + 2] = q.z;
+      w[4 * u + 3] = q.w;
+    }
+    int pos = 31;
+#pragma unroll
+    for (int pp = 15; pp >= 0; --pp) {
+      if (Pack2<T>::hi(w[pp]) == val) pos = 2 * pp + 1;
+      if (Pack2<T>::lo(w[pp]) == val) pos = 2 * pp;
+    }
+    idx = chunk * 32 + pos;
+  }
+};
+
 template <typename T, int MODE>
 struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
   float best[kChains];
@@ -284,17 +363,28 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
 };
 
 // --------------------------------------------------------------------- kernel
-template <typename T, int MODE, bool XRES, int STAGES, bool FUSE>
-__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
+template <typename T, int MODE, bool XRES, int STAGES, bool FUSE, int EPI>
+__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI>::threads, 1)
     assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
-  using L = Layout<MODE, XRES, STAGES, FUSE>;
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI>;
+  constexpr int kEpiWarps = EPI;
+  constexpr int kGroups = L::kGroups;
+  constexpr int kGCols = kCent / kGroups;   // columns per group
+  constexpr int kGChunks = kGCols / 32;     // 32-column TMEM loads per group
+  constexpr int kConvWarp0 = kEpiWarp0 + EPI;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Each CTA takes a contiguous range of (batch, 128-point) tiles, so at any
+  // moment the CTAs stream different batches' centroid tiles; round-robin
+  // assignment made all CTAs hit the same batch's centroids in the same L2
+  // slices at once.
+  const int t_begin = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.total_tiles) / gridDim.x);
+  const int t_end = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.total_tiles) / gridDim.x);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar_off);
   uint64_t* x_full = bars;
@@ -303,8 +393,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
   uint64_t* c_empty = c_full + STAGES;
   uint64_t* conv_full = c_empty + STAGES;
   uint64_t* acc_full = conv_full + STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* merge_full = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + kAcc;
+  uint64_t* merge_full = acc_empty + kAcc;
   uint64_t* merge_empty = merge_full + 2;
   uint64_t* lab_full = merge_empty + 2;
   uint64_t* lab_empty = lab_full + 2;
@@ -319,13 +409,15 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
       // (the points' rows) before it may be overwritten
       mbar_init(&x_empty[i], FUSE ? 1 + 128 : 1);
     }
+    for (int i = 0; i < kAcc; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps * 32);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&lab_full[i], 128);
       mbar_init(&lab_empty[i], 128);
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiWarps * 32);
-      mbar_init(&merge_full[i], 4 * 32);
-      mbar_init(&merge_empty[i], 4 * 32);
+      mbar_init(&merge_full[i], (kGroups - 1) * 128);
+      mbar_init(&merge_empty[i], 128);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&c_full[s], 1);
@@ -360,7 +452,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
       int last_xpar[3] = {-1, -1, -1};
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int t = t_begin; ok && t < t_end; ++t) {
         const int b = t / p.ntn;
         const int row0 = (t % p.ntn) * kRows;
         if constexpr (XRES) {
@@ -410,7 +502,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
       int ab = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int t = t_begin; ok && t < t_end; ++t) {
         if constexpr (XRES) {
           if (!mbar_wait(&x_full[xb], xph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
             ok = false;
@@ -460,7 +552,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
           }
           if (!ok) break;
           mma_commit(&acc_full[ab]);
-          if (++ab == 2) { ab = 0; aph ^= 1; }
+          if (++ab == kAcc) { ab = 0; aph ^= 1; }
         }
         if constexpr (XRES) {
           if (ok) {
@@ -477,90 +569,127 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
     // ------------------------------------------------------------- epilogue
     const int ew = warp - kEpiWarp0;
     const int q = warp & 3;          // TMEM lane quarter this warp may access
-    const int h = ew >> 2;           // which 128-column half of each tile
+    const int h = ew >> 2;           // column group: kGCols columns of each tile
     const int row = q * 32 + lane;   // point within the tile
     uint2* merge = reinterpret_cast<uint2*>(smem + L::merge_off);
     int ab = 0;
     uint32_t aph = 0;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++it) {
+    for (int t = t_begin; ok && t < t_end; ++t, ++it) {
       const int b = t / p.ntn;
       const int n = (t % p.ntn) * kRows + row;
       const bool valid = n < p.N;
       const float xsq_f = valid ? load_f(p.xsq, b * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
 
-      using Argmin = typename std::conditional<MODE == 0, ArgminPacked<T>, ArgminF32<T, MODE>>::type;
+      using Argmin = typename std::conditional<MODE == 0, ArgminSaved<T>, ArgminF32<T, MODE>>::type;
       Argmin am;
-      am.init();
+      if constexpr (MODE == 0)
+        am.init(reinterpret_cast<uint4*>(smem + L::save_off) + ew * 32 + lane, L::save_stride);
+      else
+        am.init();
       uint32_t xsq2 = 0u;
       if constexpr (MODE == 0) xsq2 = Pack2<T>::splat(xsq_f);  // exact: x_sq holds a T value
       const uint8_t* csq_row =
           static_cast<const uint8_t*>(p.csq) +
           static_cast<size_t>(b) * p.kpad * (MODE == 0 ? 2 : 4);
 
-      for (int kt = 0; kt < p.nkt; ++kt) {
-        // warp-uniform outcome: tcgen05.ld below is .sync.aligned
-        const bool got = mbar_wait(&acc_full[ab], aph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-        if (!__all_sync(0xffffffffu, got)) {
+      // The warp's chunks of this point tile in (centroid tile, chunk) order.
+      // The TMEM load and the c_sq loads of chunk g+1 are in flight while
+      // chunk g is reduced (tcgen05.wait::ld waits for every outstanding
+      // load, so at most one is outstanding); a centroid tile's accumulator
+      // is released as soon as its last chunk is in registers.
+      // 16-byte c_sq words per chunk prefetched with the TMEM load (packed
+      // 16-bit mode only; the float32-chain modes load theirs when reducing,
+      // their register budget has no room for a second set)
+      constexpr int kCsqVec = (MODE == 0) ? 4 : 1;
+      static_assert(kGChunks % 2 == 0, "chunks per group must be even");
+      const int nchunks = p.nkt * kGChunks;
+      uint32_t va[32], vb[32];
+      uint4 ca[kCsqVec], cb[kCsqVec];
+      // Start the loads of chunk g (waiting for its accumulator first).
+      auto issue = [&](int g, uint32_t(&v)[32], uint4(&cq)[kCsqVec]) -> bool {
+        const int ch = g % kGChunks;
+        if (ch == 0) {
+          // warp-uniform outcome: tcgen05.ld is .sync.aligned
+          const bool got = mbar_wait(&acc_full[ab], aph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got)) return false;
+          tc_fence_after();
+        }
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                      static_cast<uint32_t>(ab * kCent + h * kGCols + ch * 32),
+                  v);
+        if constexpr (MODE == 0) {
+          const int col0 = (g / kGChunks) * kCent + h * kGCols + ch * 32;
+          const uint4* src = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
+#pragma unroll
+          for (int i = 0; i < kCsqVec; ++i) cq[i] = __ldg(src + i);
+        }
+        return true;
+      };
+      // Chunk g's registers have landed; hand back its accumulator if done.
+      auto landed = [&](int g, uint32_t(&v)[32]) {
+        tmem_ld_wait(v);
+        if (g % kGChunks == kGChunks - 1) {
+          tc_fence_before();
+          mbar_arrive(&acc_empty[ab]);
+          if (++ab == kAcc) { ab = 0; aph ^= 1; }
+        }
+      };
+      auto reduce = [&](int g, const uint32_t(&v)[32], const uint4(&cq)[kCsqVec]) {
+        const int col0 = (g / kGChunks) * kCent + h * kGCols + (g % kGChunks) * 32;
+        if constexpr (MODE == 0) {
+          am.chunk32(v, reinterpret_cast<const uint32_t*>(cq), xsq2, col0);
+        } else {
+          const float4* src = reinterpret_cast<const float4*>(csq_row + col0 * 4);
+          float4 c4[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) c4[i] = __ldg(src + i);
+          am.chunk32(v, reinterpret_cast<const float*>(c4), xsq_f, col0);
+        }
+      };
+      if (!issue(0, va, ca)) {
+        ok = false;
+        break;
+      }
+      landed(0, va);
+#pragma unroll 1
+      for (int g = 0; g < nchunks; g += 2) {
+        if (!issue(g + 1, vb, cb)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                               static_cast<uint32_t>(ab * kCent + h * 128);
-        // Four 32-column chunks; the TMEM load of chunk ch+1 is in flight while
-        // chunk ch is processed (va/vb alternate inside a two-chunk body).
-        auto process = [&](const uint32_t(&v)[32], int ch) {
-          const int col0 = kt * kCent + h * 128 + ch * 32;
-          if constexpr (MODE == 0) {
-            const uint4* cq = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
-            uint4 c4[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) c4[i] = __ldg(cq + i);
-            am.chunk32(v, reinterpret_cast<const uint32_t*>(c4), xsq2, col0);
-          } else {
-            const float4* cq = reinterpret_cast<const float4*>(csq_row + col0 * 4);
-            float4 c4[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) c4[i] = __ldg(cq + i);
-            am.chunk32(v, reinterpret_cast<const float*>(c4), xsq_f, col0);
-          }
-        };
-        uint32_t va[32], vb[32];
-        tmem_ld32(tbase, va);
-        tmem_ld_wait(va);
-#pragma unroll 1
-        for (int c2 = 0; c2 < 2; ++c2) {
-          tmem_ld32(tbase + (2 * c2 + 1) * 32, vb);
-          process(va, 2 * c2);
-          tmem_ld_wait(vb);
-          if (c2 == 0) tmem_ld32(tbase + 2 * 32, va);
-          process(vb, 2 * c2 + 1);
-          if (c2 == 0) tmem_ld_wait(va);
+        reduce(g, va, ca);
+        landed(g + 1, vb);
+        const bool more = g + 2 < nchunks;
+        if (more && !issue(g + 2, va, ca)) {
+          ok = false;
+          break;
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[ab]);
-        if (++ab == 2) { ab = 0; aph ^= 1; }
+        reduce(g + 1, vb, cb);
+        if (more) landed(g + 2, va);
       }
       if (!ok) break;
 
       // Per-thread winner: (value, lowest column on ties).
       float val;
       int idx;
-      am.result(val, idx);
+      if constexpr (MODE == 0)
+        am.result(val, idx, h * kGCols);
+      else
+        am.result(val, idx);
 
-      // Merge the two column halves: half 1 publishes, half 0 decides.
+      // Merge the column groups: groups 1.. publish, group 0 decides.
       const int par = it & 1;
       const uint32_t mph = static_cast<uint32_t>((it >> 1) & 1);
-      uint2* slot = merge + par * kRows + row;
-      if (h == 1) {
+      uint2* mslots = merge + par * (kGroups - 1) * kRows;
+      if (h != 0) {
         const bool got = mbar_wait(&merge_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        *slot = make_uint2(__float_as_uint(val), static_cast<uint32_t>(idx));
+        mslots[(h - 1) * kRows + row] = make_uint2(__float_as_uint(val), static_cast<uint32_t>(idx));
         mbar_arrive(&merge_full[par]);
       } else {
         const bool got = mbar_wait(&merge_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
@@ -568,14 +697,17 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
           ok = false;
           break;
         }
-        const uint2 o = *slot;
-        mbar_arrive(&merge_empty[par]);
-        const float vo = __uint_as_float(o.x);
-        const int io = static_cast<int>(o.y);
-        if (vo < val || (vo == val && io < idx)) {
-          val = vo;
-          idx = io;
+#pragma unroll
+        for (int gg = 1; gg < kGroups; ++gg) {
+          const uint2 o = mslots[(gg - 1) * kRows + row];
+          const float vo = __uint_as_float(o.x);
+          const int io = static_cast<int>(o.y);
+          if (vo < val || (vo == val && io < idx)) {
+            val = vo;
+            idx = io;
+          }
         }
+        mbar_arrive(&merge_empty[par]);
         if (valid) {
           p.out[b * p.so_b + static_cast<int64_t>(n) * p.so_n] = idx;
           if (p.counts) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
@@ -594,50 +726,48 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
     }
   } else if (FUSE && XRES) {
     // ------------------------------------------- sum warps (fused accumulation)
-    // Thread s owns row s of every tile: once the epilogue has published the
-    // tile's labels, it adds its row (still resident in the tile's x buffer,
-    // 128-byte swizzle: 16-byte unit u of row r at r*128 + ((u ^ (r % 8)) * 16)
-    // of each 64-column chunk) to sums[label] with float4 atomics, then
-    // releases the x buffer.  Runs concurrently with the next tile's epilogue.
+    // Sum warp w adds rows 32w..32w+31 of every tile, one point at a time:
+    // lane l takes columns 4l..4l+3 of the point's row (still resident in the
+    // tile's x buffer, 128-byte swizzle: 16-byte unit u of row r sits at
+    // r*128 + ((u ^ (r % 8)) * 16) of each 64-column chunk), so one float4
+    // atomic instruction covers 512 contiguous bytes of sums[label] (16 full
+    // sectors) instead of 32 scattered half-sectors.  Once its labels are
+    // read the warp releases the label slot; after its rows it releases the x
+    // buffer.  Runs concurrently with the next tile's epilogue.
     if constexpr (FUSE && XRES && sizeof(T) == 2) {
-    const int srow = threadIdx.x - kConvWarp0 * 32;  // 0..127
+    const int sw = warp - kConvWarp0;  // 0..3
+    const int col = 4 * lane;
+    const int dc = col / p.dch;
+    const int ub = (col % p.dch) * 2;  // byte of column `col` within its chunk
+    const bool lane_on = col < p.D;
+    const bool lane_vec = p.sums_vec && col + 4 <= p.D;
     int it = 0, xi = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++it) {
+    for (int t = t_begin; t < t_end; ++t, ++it) {
       const int b = t / p.ntn;
       const int par = it & 1;
       const uint32_t mph = static_cast<uint32_t>((it >> 1) & 1);
       const bool got = mbar_wait(&lab_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
       if (!__all_sync(0xffffffffu, got)) break;
-      const int lab = reinterpret_cast<const int*>(smem + L::lab_off)[par * kRows + srow];
+      const int lab_mine = reinterpret_cast<const int*>(smem + L::lab_off)[par * kRows + sw * 32 + lane];
       mbar_arrive(&lab_empty[par]);
-      if (lab >= 0) {
-        float* dst = p.sums + (static_cast<int64_t>(b) * p.K + lab) * p.D;
-        const uint8_t* xbuf = smem + L::x_off + xi * kResidentChunks * kXChunk;
-        for (int dc = 0; dc < p.nd; ++dc) {
-          const uint8_t* seg = xbuf + dc * kXChunk + srow * kChunkB;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int col = dc * p.dch + u * 8;
-            if (col < p.D) {
-              const uint4 q4 = *reinterpret_cast<const uint4*>(seg + ((u ^ (srow & 7)) * 16));
-              const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
-              float f[8];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                f[2 * e] = Pack2<T>::lo(w4[e]);
-                f[2 * e + 1] = Pack2<T>::hi(w4[e]);
-              }
-              if (p.sums_vec && col + 8 <= p.D) {
-                atomicAdd(reinterpret_cast<float4*>(dst + col), make_float4(f[0], f[1], f[2], f[3]));
-                atomicAdd(reinterpret_cast<float4*>(dst + col + 4), make_float4(f[4], f[5], f[6], f[7]));
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  if (col + e < p.D) atomicAdd(dst + col + e, f[e]);
-              }
-            }
-          }
+      const uint8_t* xsrc = smem + L::x_off + (xi * kResidentChunks + dc) * kXChunk + (ub & 15);
+      float* const sums_b = p.sums + static_cast<int64_t>(b) * p.K * p.D + col;
+#pragma unroll 4
+      for (int i = 0; i < 32; ++i) {
+        const int lab = __shfl_sync(0xffffffffu, lab_mine, i);
+        if (lab < 0 || !lane_on) continue;
+        const int r = sw * 32 + i;
+        const uint2 q = *reinterpret_cast<const uint2*>(xsrc + r * kChunkB + (((ub >> 4) ^ (r & 7)) << 4));
+        const float f0 = Pack2<T>::lo(q.x), f1 = Pack2<T>::hi(q.x);
+        const float f2 = Pack2<T>::lo(q.y), f3 = Pack2<T>::hi(q.y);
+        float* dst = sums_b + static_cast<int64_t>(lab) * p.D;
+        if (lane_vec) {
+          atomicAdd(reinterpret_cast<float4*>(dst), make_float4(f0, f1, f2, f3));
+        } else {
+          atomicAdd(dst, f0);
+          if (col + 1 < p.D) atomicAdd(dst + 1, f1);
+          if (col + 2 < p.D) atomicAdd(dst + 2, f2);
+          if (col + 3 < p.D) atomicAdd(dst + 3, f3);
         }
       }
       mbar_arrive(&x_empty[xi]);
@@ -650,7 +780,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
     int stage = 0;
     uint32_t sph = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+    for (int t = t_begin; ok && t < t_end; ++t) {
       for (int kt = 0; ok && kt < p.nkt; ++kt) {
         for (int dc = 0; dc < p.nd; ++dc) {
           const bool got = mbar_wait(&c_full[stage], sph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
@@ -698,10 +828,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE>::threads, 1)
 template <typename T, int MODE, bool XRES, bool FUSE = false>
 static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
                          cudaStream_t stream) {
-  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : 4);
-  using L = Layout<MODE, XRES, STAGES, FUSE>;
+  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : 4);  // centroid ring depth
+  constexpr int EPI = 8;  // epilogue warps: 4 TMEM lane quarters x 2 column halves
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI>;
   static_assert(L::total <= 232448, "shared memory budget");
-  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE>;
+  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI>;
   const int dev = current_device();
   static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);

@@ -3,6 +3,8 @@
 Every computation here goes through the C ABI (flash_kmeans._ops -> ctypes ->
 libflashkmeans_b200.so); the oracle (numpy) is the checker only.
 """
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -87,7 +89,7 @@ def test_assign_shapes_vs_oracle(fk, dt, shape):
     from flash_kmeans import _ops
     from flash_kmeans.assign_euclid_triton import euclid_assign_triton
     B, N, K, D = shape
-    rng = np.random.default_rng(hash((dt,) + shape) % 2 ** 32)
+    rng = np.random.default_rng(zlib.crc32(repr((dt,) + shape).encode()))  # stable across runs
     x = ko.round_to(rng.standard_normal((B, N, D), dtype=np.float32), dt)
     c = ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt)
     xd = _dev(x, dt)

@@ -126,8 +126,12 @@ def test_flashkmeans_api_matches_raw(fk):
     torch.manual_seed(42)
     torch.cuda.manual_seed_all(42)
     raw, cent, _ = fk.batch_kmeans_Euclid(data, n_clusters=K, max_iters=8, tol=1e-8)
-    assert torch.equal(api, raw)
-    assert torch.equal(km.centroids_b, cent)
+    # Same seed -> same init and the same run.  Per-cluster sums are float32
+    # atomics (as in the reference's Triton update), so the two runs may differ
+    # in the last bit of a sum; compare at the parity bar, not bit for bit.
+    agree = (api == raw).float().mean().item()
+    assert agree >= 0.999, agree
+    assert_centroids(_np(km.centroids_b), _np(cent), "api vs raw")
     pred = km.predict(data)
     # predict against the final centroids differs from the training labels only by
     # the last update; it must equal a fresh assignment
