@@ -1,7 +1,7 @@
 """Benchmark of the Lloyd-iteration hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg1|cfg3|cfg4]
+                    [--workload cfg2|cfg1|cfg3|cfg4] [--op lloyd|assign]
 
 A step is one Lloyd iteration (assign + update + shift check) over the whole
 batch of the workload.  Default workload: BASELINE config 2 (B=32, N=75600,
@@ -18,6 +18,8 @@ dense bf16 peak.  `cpu_baseline`: the CPU oracle (numpy restatement of the
 reference's torch path) on a bounded sample, all host cores via a spawn pool.
 `--impl reference`: that CPU oracle alone, timed per step (the reference is a
 Python/Triton package; its CPU path is restated in oracle/).
+`--op assign`: the assignment alone (`euclid_assign_triton`, labels only, the
+predict path) per step, instead of a Lloyd iteration.
 """
 from __future__ import annotations
 
@@ -324,10 +326,63 @@ def run_ours(args, rank, world, local_rank):
                          "traffic": _load_traffic(args.workload)},
             "e2e": e2e,
             "cpu_baseline": cpu_baseline,
-            "gpu_launches": 6 * steps,
+            "gpu_launches": eng.kernels_per_step * steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+
+
+def run_assign(args, rank, world, local_rank):
+    """`--op assign`: K timed calls of euclid_assign_triton on resident inputs."""
+    import torch
+    import torch.distributed as dist
+    from flash_kmeans import _ops
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    x, c0 = _make_inputs(w, dev, seed=1234 + rank)
+    x_sq = _ops.row_sqnorm(x)
+    out = torch.empty((w["B"], w["N"]), dtype=torch.int32, device=dev)
+    for _ in range(args.warmup):
+        euclid_assign_triton(x, c0, x_sq, out=out)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            euclid_assign_triton(x, c0, x_sq, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    flops = _flops(w)
+    achieved = flops / (ms * 1e-3) / 1e12
+    burst, sustained, _, src = _peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "assign TFLOP/s (euclid_assign_triton, labels only)",
+            "value": round(achieved * world, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16" if w["dtype"] == "float16" else w["dtype"],
+            "data": "synthetic (seeded torch generator; shapes/distribution of the BASELINE config)",
+            "config": {"workload": _describe(args.workload, w),
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "step": "one euclid_assign_triton call (c_sq staging + assignment)"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst,
+                         "unit": UNIT, "frac": round(achieved / burst, 4),
+                         "peak_source": f"{src} dense bf16 (burst)",
+                         "traffic": _load_traffic(f"plain_{args.workload}")},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }), flush=True)
 
 
 # ------------------------------------------------------------- reference arm
@@ -363,6 +418,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["lloyd", "assign"], default="lloyd")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -381,7 +437,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        (run_assign if args.op == "assign" else run_ours)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -2,21 +2,22 @@
 // _euclid_assign_kernel_split_d, flash_kmeans/assign_euclid_triton.py:804-1030).
 //
 // One persistent CTA per SM walks a contiguous range of (batch, 128-point tile)
-// work items.  Per
-// item it streams the batch's centroids in tiles of 256 through a TMA ring and
-// computes the 128 x 256 cross products x.c^T with tcgen05.mma into one of
-// two TMEM accumulators (2 x 256 of the 512 columns), so the epilogue of tile
-// j overlaps the MMAs of tile j+1.  The epilogue reads its TMEM lane (= its
-// point) with tcgen05.ld, forms the distance with the reference torch path's
-// rounding and keeps a running argmin; the (B,N,K) distance matrix never
-// exists.  Nothing is written but one int32 label per point (and, optionally,
-// +1 on that label's count).
+// work items (contiguous, so the CTAs stream different batches' centroids at
+// any moment).  Per item it streams the batch's centroids in tiles of 256
+// through a TMA ring and computes the 128 x 256 cross products x.c^T with
+// tcgen05.mma into one of two TMEM accumulators (2 x 256 of the 512 columns),
+// so the epilogue of tile j overlaps the MMAs of tile j+1.  The epilogue reads
+// its TMEM lane (= its point) with tcgen05.ld, 32 columns at a time with the
+// next chunk's load in flight, forms the distance with the reference torch
+// path's rounding and keeps a running argmin; the (B,N,K) distance matrix
+// never exists.  Nothing is written but one int32 label per point (and,
+// optionally, +1 on that label's count, or with fused accumulation the point's
+// row added to its cluster's float32 sum).
 //
 // Roles (warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
-// 2..(2+EPI-1) = epilogue (warp w reads TMEM lanes 32*(w%4).. and column
-// group (w-2)/4 of each 256-column tile; EPI = 16 for 16-bit inputs, 8 for
-// float32), then 4 more warps: f32 split converters (3xTF32 mode) or sum
-// warps (fused accumulation).
+// 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4).. and column half
+// (w-2)/4 of each 256-column tile), then 4 more warps: f32 split converters
+// (3xTF32 mode) or sum warps (fused accumulation).
 //
 // Modes:
 //   0  16-bit x with x_sq in the same dtype: dist = r(r(x_sq - 2 r(x.c)) + c_sq),
@@ -186,67 +187,15 @@ __device__ __forceinline__ float round16(float v) {
   return Elem<T>::round(v);
 }
 
-// Running argmin over a thread's row, split into kChains independent chains
-// (column pair p goes to chain p % kChains) so consecutive updates do not
-// wait on each other.  Columns are visited in increasing order within a
-// chain and updates need a strictly smaller value, so each chain keeps its
-// lowest-index minimum; result() merges the chains by (value, index).
-// A chain remembers the local position of its best column inside its
-// 32-column chunk plus the chunk id, which is refreshed once per chunk where
-// the best value changed (compared as values, so -0/+0 are one value).
+// Running argmin over a thread's row for the float32-chain modes, split into
+// kChains independent chains (column j goes to chain j % kChains) so
+// consecutive updates do not wait on each other.  Columns are visited in
+// increasing order within a chain and updates need a strictly smaller value,
+// so each chain keeps its lowest-index minimum; result() merges the chains by
+// (value, index).  A chain remembers the local position of its best column
+// inside its 32-column chunk plus the chunk id, which is refreshed once per
+// chunk where the best value changed.
 constexpr int kChains = 4;
-
-template <typename T>
-struct ArgminPacked {  // mode 0: two columns per 32-bit register
-  uint32_t best[kChains], loc[kChains], chunk[kChains];
-  __device__ __forceinline__ void init() {
-#pragma unroll
-    for (int c = 0; c < kChains; ++c) {
-      best[c] = Pack2<T>::kInf2;
-      loc[c] = 0;
-      chunk[c] = 0;
-    }
-  }
-  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint32_t* cw,
-                                          uint32_t xsq2, int col0) {
-    uint32_t prev[kChains];
-#pragma unroll
-    for (int c = 0; c < kChains; ++c) prev[c] = best[c];
-#pragma unroll
-    for (int pp = 0; pp < 16; ++pp) {
-      const int c = pp % kChains;
-      const uint32_t d =
-          Pack2<T>::dist(__uint_as_float(v[2 * pp]), __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
-      const uint32_t m = Pack2<T>::lt_mask(d, best[c]);
-      best[c] = Pack2<T>::min2(best[c], d);
-      loc[c] = ((static_cast<uint32_t>(pp) * 0x00010001u) & m) | (loc[c] & ~m);
-    }
-    const uint32_t cid2 = static_cast<uint32_t>(col0 >> 5) * 0x00010001u;
-#pragma unroll
-    for (int c = 0; c < kChains; ++c) {
-      const uint32_t chg = Pack2<T>::ne_mask(best[c], prev[c]);
-      chunk[c] = (cid2 & chg) | (chunk[c] & ~chg);
-    }
-  }
-  __device__ __forceinline__ void result(float& val, int& idx) const {
-    val = __int_as_float(0x7f800000);
-    idx = 0x7fffffff;
-#pragma unroll
-    for (int c = 0; c < kChains; ++c) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float v = e ? Pack2<T>::hi(best[c]) : Pack2<T>::lo(best[c]);
-        const uint32_t ch = e ? (chunk[c] >> 16) : (chunk[c] & 0xFFFFu);
-        const uint32_t lo = e ? (loc[c] >> 16) : (loc[c] & 0xFFFFu);
-        const int i = static_cast<int>((ch << 5) + (lo << 1)) + e;
-        if (v < val || (v == val && i < idx)) {
-          val = v;
-          idx = i;
-        }
-      }
-    }
-  }
-};
 
 // Running argmin for mode 0 that spends about one ALU operation per column
 // pair: each 32-column chunk is reduced to its minimum with a tree of packed
@@ -576,11 +525,19 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI>::threads
     uint32_t aph = 0;
     int it = 0;
     bool ok = true;
+    // x_sq of this thread's point in tile t (0 past N), fetched one tile
+    // ahead so the tile's first distances do not wait on an HBM read
+    auto load_xsq = [&](int t) -> float {
+      const int n = (t % p.ntn) * kRows + row;
+      return n < p.N ? load_f(p.xsq, (t / p.ntn) * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
+    };
+    float xsq_next = t_begin < t_end ? load_xsq(t_begin) : 0.0f;
     for (int t = t_begin; ok && t < t_end; ++t, ++it) {
       const int b = t / p.ntn;
       const int n = (t % p.ntn) * kRows + row;
       const bool valid = n < p.N;
-      const float xsq_f = valid ? load_f(p.xsq, b * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
+      const float xsq_f = xsq_next;
+      if (t + 1 < t_end) xsq_next = load_xsq(t + 1);
 
       using Argmin = typename std::conditional<MODE == 0, ArgminSaved<T>, ArgminF32<T, MODE>>::type;
       Argmin am;
@@ -1073,7 +1030,18 @@ extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq,
 // is read once per Lloyd iteration.  Other layouts: fk_assign with a workspace
 // histogram followed by fk_centroid_accumulate (counting-sort path).
 // ---------------------------------------------------------------------------
-static bool assign_accumulate_fused(int64_t D, int dtype) {
+// How fk_assign_accumulate accumulates:
+//   privatised: K x D small enough for shared memory; fk_assign (labels only)
+//     then the privatised segmented sum, which reads x a second time but adds
+//     each CTA's partial sums to the global ones once (with small K the fused
+//     kernel's per-point atomics would pile onto a few cluster rows);
+//   fused: 16-bit x with D <= 128, the sum warps of the assignment kernel add
+//     each point's resident row (x read once);
+//   sorted: otherwise fk_assign then fk_centroid_accumulate's counting sort.
+static bool assign_accumulate_priv(int64_t K, int64_t D) { return segsum_priv_fits(K, D); }
+
+static bool assign_accumulate_fused(int64_t K, int64_t D, int dtype) {
+  if (assign_accumulate_priv(K, D)) return false;
   if (dtype != FK_F16 && dtype != FK_BF16) return false;
   const int64_t nd = (D * 2 + kChunkB - 1) / kChunkB;
   return nd <= kResidentChunks;
@@ -1082,7 +1050,7 @@ static bool assign_accumulate_fused(int64_t D, int dtype) {
 extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                       int dtype) {
   const size_t wa = fk_assign_workspace_size(B, K, dtype);
-  if (assign_accumulate_fused(D, dtype)) return wa;
+  if (assign_accumulate_priv(K, D) || assign_accumulate_fused(K, D, dtype)) return wa;
   return wa + align_up(static_cast<size_t>(B > 0 && K > 0 ? B * K : 1) * 4, 256) +
          fk_centroid_accumulate_workspace_size(B, N, K);
 }
@@ -1103,7 +1071,15 @@ extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const 
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(FK_ERR_WORKSPACE, "fk_assign_accumulate: workspace needs %zu bytes, 256-aligned", need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (!assign_accumulate_fused(D, dtype)) {
+  if (assign_accumulate_priv(K, D)) {
+    int st = fk_assign(x, centroids, x_sq, c_sq, out, nullptr, dtype, xsq_dtype, csq_dtype, B, N, K,
+                       D, x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2,
+                       workspace, workspace_bytes, dev_status, stream);
+    if (st != FK_OK) return st;
+    return segsum_priv(x, dtype, x_strides3, out, FK_I32, out_strides2, B, N, K, D, sums, counts,
+                       dev_status, s);
+  }
+  if (!assign_accumulate_fused(K, D, dtype)) {
     const size_t wa = fk_assign_workspace_size(B, K, dtype);
     int32_t* hist = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + wa);
     void* wu = static_cast<uint8_t*>(workspace) + wa + align_up(static_cast<size_t>(B * K) * 4, 256);

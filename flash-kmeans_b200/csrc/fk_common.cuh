@@ -92,4 +92,12 @@ int encode_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, u
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Privatised centroid accumulation (fk_update.cu): true when one batch's
+// K x D float32 sums and K counts fit in a CTA's shared memory.
+bool segsum_priv_fits(int64_t K, int64_t D);
+// sums[b][ids] += rows of x; counts[b][ids] += 1 unless counts is null.
+int segsum_priv(const void* x, int dtype, const int64_t* xs, const void* ids, int ids_dtype,
+                const int64_t* is, int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
+                int32_t* counts, int32_t* status, cudaStream_t s);
+
 }  // namespace fk

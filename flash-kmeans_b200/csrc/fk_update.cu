@@ -8,8 +8,12 @@
 // scan -> scatter of point indices.  A segmented-sum kernel then walks the
 // sorted order 32 points per warp, each lane owning 4 consecutive columns,
 // accumulating in float32 registers and flushing one (vector) atomic per run
-// boundary.  The finalize kernel divides, keeps empty clusters, casts, and
-// also produces the next iteration's ||c||^2 and the centre shift.
+// boundary.  When one batch's K x D float32 sums fit in shared memory no sort
+// is needed: each CTA accumulates its contiguous range of points privately in
+// shared memory and adds its partial sums to the global ones once.  The
+// finalize kernel divides, keeps empty clusters, casts, and also produces the
+// next iteration's ||c||^2 and the centre shift.
+#include <algorithm>
 #include <type_traits>
 
 #include "fk_common.cuh"
@@ -505,6 +509,310 @@ static int hist_scatter(const void* ids, const int64_t* is, int64_t B, int64_t N
   return check_launch("scatter_kernel");
 }
 
+
+// ------------------------------------------------ privatised segmented sum
+// For K x D small enough that a batch's float32 sums (and K counts) fit in
+// shared memory.  CTA c takes the contiguous point range
+// [c*total/grid, (c+1)*total/grid) of the flattened (B, N) points, one batch
+// segment at a time, in chunks of kPrivChunk points:
+//   A. labels are read (coalesced) and counted per cluster with
+//      warp-aggregated shared atomics (__match_any_sync: one atomic per
+//      distinct label of a warp), each point getting its slot in its bin;
+//   B. one warp scans the bins (and adds them to the private counts);
+//   C. the chunk's point indices are scattered into label order;
+//   D. each warp walks a contiguous range of that order, loading rows 4 at a
+//      time (each lane 4 consecutive columns of a 128-column group) and
+//      summing them in registers, with one shared-memory flush per run of
+//      equal labels.
+// Float atomics thus happen once per run, not once per point, so clusters
+// holding most of the points (skewed data) cost least instead of
+// serialising.  At the end of a segment the private sums are added to the
+// global ones (one vector atomic per non-zero group of 4) and the counts with
+// one atomic each.  x is read once.  The private rows are padded to a
+// multiple of 128 columns and each 128-column group is stored transposed
+// (column 4i+e at slot 32e+i) so a warp's flush touches 32 consecutive words
+// per instruction.
+constexpr int kPrivThreads = 512;
+constexpr int kPrivChunk = 2048;
+constexpr size_t kPrivMaxSmem = 200 * 1024;
+static_assert(kPrivChunk % kPrivThreads == 0, "chunk must be a multiple of the block");
+
+static int64_t priv_row(int64_t D) { return (D + 127) / 128 * 128; }
+
+static size_t priv_smem_bytes(int64_t K, int64_t D) {
+  return static_cast<size_t>(K * priv_row(D) + 3 * K + 3 * kPrivChunk + 4) * 4;
+}
+
+bool segsum_priv_fits(int64_t K, int64_t D) {
+  return D <= 512 && priv_smem_bytes(K, D) <= kPrivMaxSmem;
+}
+
+// Four consecutive columns d..d+3 of a row as float (missing ones 0).
+template <typename T>
+__device__ __forceinline__ void load4_f(const T* row, int d, int D, int64_t sxd, bool vec,
+                                        float (&f)[4]) {
+  if (vec) {  // D % 4 == 0, unit stride, 4-element aligned rows
+    if constexpr (std::is_same<T, float>::value) {
+      const float4 v = *reinterpret_cast<const float4*>(row + d);
+      f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2*>(row + d);
+      const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_f(h[e]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f[e] = d + e < D ? Elem<T>::to_f(row[(d + e) * sxd]) : 0.f;
+  }
+}
+
+// NG = number of 128-column groups of a row (1, 2 or 4).
+template <typename T, typename I, int NG>
+__global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
+    const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd, const I* __restrict__ ids,
+    int64_t sib, int64_t sin, int N, int K, int D, int64_t total, float* __restrict__ sums,
+    int32_t* __restrict__ counts, bool vec_x, bool vec_sums, int* status) {
+  extern __shared__ float priv_sh[];
+  const int R = (D + 127) / 128 * 128;  // padded row
+  float* ssum = priv_sh;                                                  // [K][R]
+  int* scnt = reinterpret_cast<int*>(priv_sh + static_cast<size_t>(K) * R);  // [K]
+  int* bin = scnt + K;                                                    // [K]
+  int* start = bin + K;                                                   // [K]
+  int* slab = start + K;                                                  // [chunk] label
+  int* sslot = slab + kPrivChunk;                                         // [chunk] slot in bin
+  int* perm = sslot + kPrivChunk;                                         // [chunk] sorted
+  int* s_nvalid = perm + kPrivChunk;
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * total / gridDim.x;
+  const int64_t end = static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int KD = K * D;
+  const int KR = K * R;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) bin[k] = 0;
+  int64_t p0 = begin;
+  while (p0 < end) {
+    const int b = static_cast<int>(p0 / N);
+    const int64_t p1 = min(end, static_cast<int64_t>(b + 1) * N);  // this batch's part
+    for (int i = threadIdx.x; i < KR; i += blockDim.x) ssum[i] = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) scnt[k] = 0;
+    __syncthreads();
+    const T* xb = x + static_cast<int64_t>(b) * sxb;
+    const I* ib = ids + static_cast<int64_t>(b) * sib;
+    for (int64_t c0 = p0; c0 < p1; c0 += kPrivChunk) {
+      const int P = static_cast<int>(p1 - c0 < kPrivChunk ? p1 - c0 : kPrivChunk);
+      const int64_t n0 = c0 - static_cast<int64_t>(b) * N;  // chunk start within the batch
+      // A. labels (all of this thread's loads issued first), bin counts, slots
+      constexpr int kPer = kPrivChunk / kPrivThreads;
+      int64_t lraw[kPer];
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int j = r * kPrivThreads + threadIdx.x;
+        lraw[r] = j < P ? static_cast<int64_t>(ib[(n0 + j) * sin]) : -1;
+      }
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int j = r * kPrivThreads + threadIdx.x;
+        int lab = -1;
+        if (j < P) {
+          const int64_t l = lraw[r];
+          if (l >= 0 && l < K) lab = static_cast<int>(l);
+          else if (status) atomicCAS(status, 0, FK_DEV_BAD_LABEL);
+          slab[j] = lab;
+        }
+        const unsigned act = __ballot_sync(0xffffffffu, lab >= 0);
+        if (lab >= 0) {
+          const unsigned grp = __match_any_sync(act, lab);
+          const int leader = __ffs(grp) - 1;
+          int base = 0;
+          if (lane == leader) base = atomicAdd(&bin[lab], __popc(grp));
+          base = __shfl_sync(grp, base, leader);
+          sslot[j] = base + __popc(grp & ((1u << lane) - 1u));
+        }
+      }
+      __syncthreads();
+      // B. exclusive scan of the bins
+      if (warp == 0) {
+        int carry = 0;
+        for (int k0 = 0; k0 < K; k0 += 32) {
+          const int k = k0 + lane;
+          const int v = k < K ? bin[k] : 0;
+          int incl = v;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          if (k < K) {
+            start[k] = carry + incl - v;
+            scnt[k] += v;
+            bin[k] = 0;
+          }
+          carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) *s_nvalid = carry;
+      }
+      __syncthreads();
+      // C. scatter into label order
+      for (int j = threadIdx.x; j < P; j += blockDim.x) {
+        const int lab = slab[j];
+        if (lab >= 0) perm[start[lab] + sslot[j]] = j;
+      }
+      __syncthreads();
+      // D. runs of equal labels, summed in registers
+      const int nv = *s_nvalid;
+      const int per = (nv + nwarps - 1) / nwarps;
+      const int q0 = warp * per;
+      const int q1 = min(nv, q0 + per);
+      float acc[NG][4];
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+      int cur = -1;
+      auto flush = [&]() {
+        float* dst = ssum + cur * R + lane;  // slot 32e + lane of each group
+#pragma unroll
+        for (int g = 0; g < NG; ++g)
+          if (g * 128 + lane * 4 < D) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              atomicAdd(dst + g * 128 + 32 * e, acc[g][e]);
+              acc[g][e] = 0.f;
+            }
+          }
+      };
+      // rows loaded per warp before summing (more would lower occupancy)
+      constexpr int kB = 4;
+      for (int q = q0; q < q1; q += kB) {
+        float f[kB][NG][4];
+        int lab[kB];
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          lab[u] = -1;
+          if (q + u < q1) {
+            const int j = perm[q + u];
+            lab[u] = slab[j];
+            const T* row = xb + (n0 + j) * sxn;
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+              const int d = g * 128 + lane * 4;
+              if (d < D) load4_f<T>(row, d, D, sxd, vec_x, f[u][g]);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          if (lab[u] < 0) continue;
+          if (lab[u] != cur) {
+            if (cur >= 0) flush();
+            cur = lab[u];
+          }
+#pragma unroll
+          for (int g = 0; g < NG; ++g)
+            if (g * 128 + lane * 4 < D) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[g][e] += f[u][g][e];
+            }
+        }
+      }
+      if (cur >= 0) flush();
+      __syncthreads();
+    }
+    // private slot of (cluster k, column d): k*R + (d & ~127) + 32*(d & 3) + (d & 127)/4
+    float* gs = sums + static_cast<int64_t>(b) * KD;
+    if (vec_sums && D % 4 == 0) {
+      for (int i = threadIdx.x * 4; i < KD; i += blockDim.x * 4) {
+        const int k = i / D, d = i - k * D;  // d % 4 == 0
+        const float* src = ssum + k * R + (d & ~127) + ((d & 127) >> 2);
+        const float4 v = make_float4(src[0], src[32], src[64], src[96]);
+        if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f)
+          atomicAdd(reinterpret_cast<float4*>(gs + i), v);
+      }
+    } else {
+      for (int i = threadIdx.x; i < KD; i += blockDim.x) {
+        const int k = i / D, d = i - k * D;
+        const float v = ssum[k * R + (d & ~127) + 32 * (d & 3) + ((d & 127) >> 2)];
+        if (v != 0.f) atomicAdd(gs + i, v);
+      }
+    }
+    if (counts) {
+      int32_t* gc = counts + static_cast<int64_t>(b) * K;
+      for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int c = scnt[k];
+        if (c) atomicAdd(gc + k, c);
+      }
+    }
+    __syncthreads();
+    p0 = p1;
+  }
+}
+
+template <typename T, typename I, int NG>
+static int launch_priv_ng(const void* x, const int64_t* xs, const void* ids, const int64_t* is,
+                          int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
+                          int32_t* counts, int32_t* status, cudaStream_t s) {
+  const size_t smem = priv_smem_bytes(K, D);
+  auto kern = segsum_priv_kernel<T, I, NG>;
+  static bool attr_done[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "segsum_priv: no current device");
+  if (!attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kPrivMaxSmem));
+    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "segsum_priv attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPrivThreads, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int sms = sm_count_current();
+  const int64_t total = B * N;
+  int64_t grid = static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm;
+  // each CTA zeroes and flushes K x D values per batch segment: keep a few
+  // chunks of points per CTA at least
+  grid = std::min<int64_t>(grid, std::max<int64_t>(1, total / (2 * kPrivChunk)));
+  const bool vec_x = xs[2] == 1 && D % 4 == 0 &&
+                     reinterpret_cast<uintptr_t>(x) % (4 * sizeof(T)) == 0 &&
+                     (xs[1] * static_cast<int64_t>(sizeof(T))) % (4 * sizeof(T)) == 0 &&
+                     (xs[0] * static_cast<int64_t>(sizeof(T))) % (4 * sizeof(T)) == 0;
+  const bool vec_sums = (K * D) % 4 == 0 && reinterpret_cast<uintptr_t>(sums) % 16 == 0;
+  kern<<<static_cast<int>(grid), kPrivThreads, smem, s>>>(
+      static_cast<const T*>(x), xs[0], xs[1], xs[2], static_cast<const I*>(ids), is[0], is[1],
+      static_cast<int>(N), static_cast<int>(K), static_cast<int>(D), total, sums, counts, vec_x,
+      vec_sums, status);
+  return check_launch("segsum_priv_kernel");
+}
+
+template <typename T, typename I>
+static int launch_priv_typed(const void* x, const int64_t* xs, const void* ids, const int64_t* is,
+                             int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
+                             int32_t* counts, int32_t* status, cudaStream_t s) {
+  if (D <= 128) return launch_priv_ng<T, I, 1>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  if (D <= 256) return launch_priv_ng<T, I, 2>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  return launch_priv_ng<T, I, 4>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+}
+
+int segsum_priv(const void* x, int dtype, const int64_t* xs, const void* ids, int ids_dtype,
+                const int64_t* is, int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
+                int32_t* counts, int32_t* status, cudaStream_t s) {
+  const bool i32 = ids_dtype == FK_I32;
+  switch (dtype) {
+    case FK_F16:
+      return i32 ? launch_priv_typed<__half, int32_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s)
+                 : launch_priv_typed<__half, int64_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+    case FK_BF16:
+      return i32 ? launch_priv_typed<__nv_bfloat16, int32_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s)
+                 : launch_priv_typed<__nv_bfloat16, int64_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+    case FK_F32:
+      return i32 ? launch_priv_typed<float, int32_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s)
+                 : launch_priv_typed<float, int64_t>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+    default:
+      return fail(FK_ERR_INVALID_ARG, "segsum_priv: unsupported dtype %d", dtype);
+  }
+}
+
 template <typename T>
 static int bulk_smem_attr(int nsub, int smem) {
   static bool done[4][64] = {};
@@ -613,10 +921,18 @@ extern "C" int fk_centroid_accumulate(const void* x, int dtype, int64_t B, int64
     return fail(FK_ERR_INVALID_ARG, "fk_centroid_accumulate: ids must be int32 or int64");
   if (N >= (1ll << 31) || K >= (1ll << 31) || B >= 65536)
     return fail(FK_ERR_UNSUPPORTED, "fk_centroid_accumulate: sizes exceed kernel limits");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype != FK_F16 && dtype != FK_BF16 && dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "fk_centroid_accumulate: unsupported dtype %d", dtype);
+  if (segsum_priv_fits(K, D)) {
+    // no sort needed; `hist`, when given, is the histogram of these very ids,
+    // so counting here adds the same numbers to `counts`
+    return segsum_priv(x, dtype, x_strides3, ids, ids_dtype, ids_strides2, B, N, K, D, sums,
+                       counts == hist ? nullptr : counts, dev_status, s);
+  }
   const size_t need = fk_centroid_accumulate_workspace_size(B, N, K);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(FK_ERR_WORKSPACE, "fk_centroid_accumulate: workspace needs %zu bytes", need);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   const size_t bk = align_up(static_cast<size_t>(B * K) * 4, 256);
   const size_t bn = align_up(static_cast<size_t>(B * N) * 4, 256);

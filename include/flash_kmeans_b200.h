@@ -111,8 +111,10 @@ int fk_assign(const void* x, const void* centroids, const void* x_sq, const void
  * finalize).  Same arguments as fk_assign plus `sums` (B,K,D float32
  * contiguous); `counts` (B,K int32) is required.  Labels are written to `out`,
  * their histogram is ADDED to `counts` and the rows of x are ADDED to
- * sums[label].  With 16-bit x and D <= 128 this is one kernel that reads x
- * once; otherwise it runs fk_assign then fk_centroid_accumulate. */
+ * sums[label].  When a batch's K x D float32 sums (plus K counts) fit in
+ * 200 KiB of shared memory it runs fk_assign then the privatised sum of
+ * fk_centroid_accumulate; else with 16-bit x and D <= 128 it is one kernel
+ * that reads x once; otherwise fk_assign then fk_centroid_accumulate. */
 size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
 int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
                          int32_t* out, int32_t* counts, float* sums, int dtype, int xsq_dtype,
@@ -145,8 +147,11 @@ int fk_assign_static_scratch(const void* x, const void* centroids, const void* x
  * of the rows of x grouped by ids (B,N; FK_I32 or FK_I64), ADDED to `sums`
  * and `counts`.  `hist` (B,K) optional: the histogram of exactly these ids
  * (e.g. produced by fk_assign's `counts`); NULL -> computed here.
- * Grouping is a counting sort (histogram, scan, scatter) followed by a
- * segmented sum over the sorted order. */
+ * When a batch's K x D float32 sums plus K counts fit in 200 KiB, each CTA
+ * accumulates its share of the points in shared memory and adds its partial
+ * sums once (the workspace is then unused); otherwise grouping is a counting
+ * sort (histogram, scan, scatter) followed by a segmented sum over the sorted
+ * order. */
 size_t fk_centroid_accumulate_workspace_size(int64_t B, int64_t N, int64_t K);
 int fk_centroid_accumulate(const void* x, int dtype, int64_t B, int64_t N, int64_t K, int64_t D,
                            const int64_t* x_strides3, const void* ids, int ids_dtype,

@@ -195,13 +195,47 @@ def test_update_bad_label_reports_device_status(fk):
     assert int(cnt.sum()) == 63
 
 
+def _torch_sums(x, ids, K):
+    """float32 per-cluster row sums and counts with torch (index_add / bincount)."""
+    B, N, D = x.shape
+    sums = torch.zeros((B, K, D), device=x.device)
+    cnts = torch.zeros((B, K), dtype=torch.int32, device=x.device)
+    for b in range(B):
+        sums[b].index_add_(0, ids[b].long(), x[b].float())
+        cnts[b] = torch.bincount(ids[b].long(), minlength=K).int()
+    return sums, cnts
+
+
+# K x D below / above the shared-memory privatisation limit (51200 floats)
+@pytest.mark.parametrize("dt,B,N,K,D,idt", [
+    ("float16", 2, 3000, 77, 128, torch.int32), ("float32", 1, 2000, 300, 100, torch.int64),
+    ("float16", 2, 3000, 600, 128, torch.int64), ("bfloat16", 1, 2500, 700, 96, torch.int32)])
+def test_accumulate_privatised_and_sorted_paths(fk, dt, B, N, K, D, idt):
+    """fk_centroid_accumulate against torch index_add: the privatised shared-memory kernel
+    (small K x D) and the counting-sort segmented sum (large K x D)."""
+    from flash_kmeans import _ops
+    g = torch.Generator(device="cuda").manual_seed(K + D)
+    x = torch.randn((B, N, D), device="cuda", generator=g).to(getattr(torch, dt))
+    ids = torch.randint(0, K, (B, N), device="cuda", generator=g).to(idt)
+    ids[:, :N // 3] = K // 2  # a crowded cluster
+    sums = torch.zeros((B, K, D), device="cuda")
+    cnts = torch.zeros((B, K), dtype=torch.int32, device="cuda")
+    _ops.accumulate(x, ids, sums, cnts)
+    ref_s, ref_c = _torch_sums(x, ids, K)
+    assert torch.equal(cnts, ref_c)
+    torch.testing.assert_close(sums, ref_s, rtol=1e-5, atol=1e-3)
+
+
 # -------------------------------------------------- fused assign + accumulate
 @pytest.mark.parametrize("dt,B,N,K,D", [
     ("float16", 3, 5000, 1000, 128), ("float16", 2, 700, 70, 64), ("bfloat16", 2, 900, 33, 100),
-    ("float16", 1, 1000, 50, 17), ("float16", 1, 640, 40, 192), ("float32", 2, 800, 60, 48)])
+    ("float16", 1, 1000, 50, 17), ("float16", 1, 640, 40, 192), ("float32", 2, 800, 60, 48),
+    ("bfloat16", 2, 900, 600, 100), ("float16", 1, 3000, 3100, 17), ("float16", 1, 640, 300, 192),
+    ("float32", 1, 1200, 1100, 48)])
 def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
-    """fk_assign_accumulate (fused for 16-bit D<=128, internal fallback otherwise) equals
-    fk_assign + fk_centroid_accumulate: labels bit-identical, counts exact, sums to fp32 order."""
+    """fk_assign_accumulate (privatised for small K x D, fused for 16-bit D<=128, sorted
+    otherwise) equals fk_assign + torch index_add: labels bit-identical, counts exact, sums
+    to fp32 order."""
     from flash_kmeans import _native as nat
     from flash_kmeans import _ops
     lib = nat.load()
@@ -210,9 +244,7 @@ def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     c = _ops.ensure_tma(_dev(ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt), dt))
     xsq = _ops.row_sqnorm(x)
     ref = _ops.assign(x, c, xsq)
-    ref_s = torch.zeros((B, K, D), device="cuda")
-    ref_c = torch.zeros((B, K), dtype=torch.int32, device="cuda")
-    _ops.accumulate(x, ref, ref_s, ref_c)
+    ref_s, ref_c = _torch_sums(x, ref, K)
     out = torch.full((B, N), -1, dtype=torch.int32, device="cuda")
     sums = torch.zeros((B, K, D), device="cuda")
     cnts = torch.zeros((B, K), dtype=torch.int32, device="cuda")
