@@ -424,9 +424,12 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
                                 int K, int D, float* __restrict__ csq_out,
                                 float* __restrict__ shift_out, bool reset, bool vec) {
   const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t wpb = blockDim.x >> 5;
   float wmax = 0.f;
-  if (r < static_cast<int64_t>(B) * K) {
+  // warp per row, grid-stride: a few hundred blocks, so the shift below costs
+  // a few hundred same-address atomics rather than one per 8 rows
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5);
+       r < static_cast<int64_t>(B) * K; r += static_cast<int64_t>(gridDim.x) * wpb) {
     const int64_t b = r / K, k = r % K;
     const int32_t cnt = counts[r];
     const float fc = static_cast<float>(cnt);
@@ -466,7 +469,7 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
     if (lane == 0) {
       if (reset) counts[r] = 0;
       if (csq_out) csq_out[r] = Elem<T>::round(cs);
-      wmax = Elem<T>::round(sqrtf(ss));
+      wmax = fmaxf(wmax, Elem<T>::round(sqrtf(ss)));
     }
   }
   // one atomic per block for the shift (non-negative floats order as uints)
@@ -983,7 +986,7 @@ extern "C" int fk_centroid_finalize(float* sums, int32_t* counts, const void* ol
   }
   if (B == 0) return FK_OK;
   const int64_t rows = B * K;
-  const int grid = static_cast<int>((rows + 7) / 8);  // one warp per row
+  const int grid = grid_for(rows, 8, 4);  // 8 rows (warps) per block, grid-stride
   const int64_t* os = old_strides3;
   const int64_t* ns = new_strides3;
   const int64_t eb = dtype_bytes(dtype);
