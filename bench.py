@@ -44,8 +44,12 @@ WORKLOADS = {
     "cfg1": dict(B=2, N=16384, D=128, K=256, dtype="float32", gen="gmm", comps=256, mean_std=2.0),
     "cfg2": dict(B=32, N=75600, D=128, K=1000, dtype="float16", gen="randn"),
     "cfg3": dict(B=1, N=1 << 22, D=128, K=128, dtype="float16", gen="gmm", comps=128,
-                 mean_std=3.0, dirichlet=True),
-    "cfg4": dict(B=1, N=262144, D=2048, K=1024, dtype="float32", gen="randn"),
+                 mean_std=3.0, dirichlet=True, cpu_n=1 << 20),
+    "cfg4": dict(B=1, N=262144, D=2048, K=1024, dtype="float32", gen="randn", cpu_n=65536),
+    # out-of-core kmeans_largeN: x in pinned host memory, streamed in BLOCK_N blocks,
+    # N partitioned contiguously over the ranks (one process per GPU)
+    "cfg5": dict(B=1, N=1 << 26, D=128, K=8192, dtype="float32", gen="randn", large=True,
+                 block=1 << 20, cpu_n=1 << 16),
 }
 
 
@@ -86,17 +90,21 @@ class CpuOracle:
 
     def step(self, seed=0):
         w = self.w
-        jobs = [(seed * 1000 + i, w["N"], w["K"], w["D"], w["dtype"]) for i in range(self.cores)]
+        jobs = [(seed * 1000 + i, w.get("cpu_n", w["N"]), w["K"], w["D"], w["dtype"])
+                for i in range(self.cores)]
         t0 = time.perf_counter()
         self.pool.map(_oracle_batch_iter, jobs)
         return time.perf_counter() - t0
 
     def tflops(self, seconds):
-        return _flops(self.w) / self.w["B"] * self.cores / seconds / 1e12
+        n = self.w.get("cpu_n", self.w["N"])
+        return 2.0 * n * self.w["K"] * self.w["D"] * self.cores / seconds / 1e12
 
     def sample(self):
-        return (f"{self.cores} of {self.w['B']} batches of the workload, one Lloyd iteration "
-                f"per step (numpy oracle, one process per core)")
+        n = self.w.get("cpu_n", self.w["N"])
+        part = "" if n == self.w["N"] else f" ({n} of their {self.w['N']} points)"
+        return (f"{self.cores} of {self.w['B']} batches of the workload{part}, one Lloyd "
+                f"iteration per step (numpy oracle, one process per core)")
 
     def close(self):
         self.pool.close()
@@ -385,6 +393,139 @@ def run_assign(args, rank, world, local_rank):
         }), flush=True)
 
 
+def run_large(args, rank, world, local_rank):
+    """cfg5: kmeans_largeN's streaming engine; one step = one Lloyd iteration over all N
+    points (every rank streams its contiguous shard from pinned host memory, partial sums
+    are all-reduced over NCCL, each rank finalizes its replica)."""
+    import torch
+    import torch.distributed as dist
+    from flash_kmeans import kmeans_large as kl
+
+    w = WORKLOADS[args.workload]
+    N, D, K, BLOCK = w["N"], w["D"], w["K"], w["block"]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    pg = dist.group.WORLD if world > 1 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuOracle(w)
+    _, ps, pe = kl.partition_blocks(N, BLOCK, world)
+    p0, p1 = ps[rank], pe[rank]
+    n = p1 - p0
+    # this rank's shard: x ~ N(0,1) generated on the GPU, kept in pinned host memory
+    x_h = torch.empty((n, D), dtype=torch.float32, pin_memory=True)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    for a in range(0, n, BLOCK):
+        b = min(n, a + BLOCK)
+        x_h[a:b].copy_(torch.randn((b - a, D), device=dev, generator=g))
+    torch.cuda.synchronize()
+    gc = torch.Generator().manual_seed(99)
+    c0 = x_h[torch.randint(0, n, (K,), generator=gc)].to(dev)
+    if world > 1:
+        kl.broadcast_centroids(c0, None)
+
+    # as kmeans_largeN: keep the shard resident in HBM after the first pass when it fits
+    resident = not args.stream and kl._fits_resident(dev, n, D, torch.float32)
+    lane = kl._DeviceLane(dev, x_h, 0, n, BLOCK, K, D, torch.float32, resident=resident)
+    with torch.cuda.device(dev), torch.cuda.stream(lane.compute_stream):
+        lane.c_cur[0].copy_(c0)
+        lane.stat.zero_()
+
+    def one_iter(wrap):
+        lane.run_pass(wrap=wrap)
+        kl._allreduce([lane], pg)
+        lane.finalize()
+        _, code = lane.read_stat()  # the reference's per-iteration shift readback
+        if code:
+            raise RuntimeError(f"device status {code}")
+        lane.advance()
+
+    for _ in range(args.warmup):
+        one_iter(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(lane.compute_stream)
+        for i in range(args.steps):
+            one_iter(i + 1 < args.steps)
+        e1.record(lane.compute_stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    flops = 2.0 * N * K * D
+    value = flops / (ms * 1e-3) / 1e12
+    burst, sustained, hbm, src = _peaks()
+    with torch.cuda.device(dev):
+        lane.copy_stream.synchronize()
+        lane.compute_stream.synchronize()
+    del lane
+    torch.cuda.empty_cache()
+
+    # e2e: the public entry point on the same host shard, labels copied back
+    e2e = None
+    if args.e2e_steps > 0:
+        iters = args.e2e_steps
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        f0 = time.perf_counter()
+        kw = dict(process_group=pg, device=dev) if world > 1 else dict(device=dev)
+        labels, cent = kl.kmeans_largeN(x_h, K, max_iters=iters, tol=-1, BLOCK_N=BLOCK,
+                                        init_centroids=c0.cpu(), **kw)
+        labels_h = labels.cpu()
+        torch.cuda.synchronize()
+        secs = time.perf_counter() - f0
+        tt = torch.tensor([secs], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(flops * iters / float(tt[0]) / 1e12, 3), "unit": UNIT,
+               "h2d_bytes_per_step": int(n * D * 4), "d2h_bytes_per_step": int(labels_h.numel() * 4 / iters),
+               "step": f"kmeans_largeN(max_iters={iters}) per rank on its pinned host shard, "
+                       "labels copied back; wall clock incl. set-up, max over ranks"}
+
+    cpu_baseline = None
+    if cpu is not None:
+        cpu.step(seed=99)
+        secs = cpu.step(seed=7)
+        cpu_baseline = {"value": round(cpu.tflops(secs), 5), "unit": UNIT, "cores": cpu.cores,
+                        "kind": "port", "sample": cpu.sample()}
+        cpu.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32(3xTF32)", "data": "synthetic (x ~ N(0,1) from a seeded torch generator, "
+                                            "pinned host memory)",
+            "config": {"workload": f"{args.workload}: kmeans_largeN N={N} D={D} K={K} float32, "
+                                   f"BLOCK_N={BLOCK}",
+                       "parallelism": f"N partitioned over {world} ranks, NCCL all-reduce of "
+                                      "K*D sums + K counts per iteration",
+                       "l2": ("x copied from host once, then resident in HBM (GBs per rank, > L2)"
+                              if resident else
+                              "x streamed from host every iteration (GBs per rank); no flush"),
+                       "step": "one streamed Lloyd iteration incl. the shift readback"},
+            "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": burst,
+                         "unit": UNIT, "frac": round(value / world / burst, 4),
+                         "peak_source": f"{src} dense bf16 (burst); fp32 runs as 3 tf32 MMAs",
+                         "traffic": None,
+                         "pcie_h2d_gbs_per_rank": (None if resident else
+                                                   round(n * D * 4 / (ms * 1e-3) / 1e9, 1))},
+            "e2e": e2e, "cpu_baseline": cpu_baseline,
+            # per block: c_sq staging, assignment, scan, scatter, segmented sum; per
+            # iteration: finalize (float32 rows with K*D too large for shared memory)
+            "gpu_launches": args.steps * (5 * ((n + BLOCK - 1) // BLOCK) + 1),
+            "clocks": clk.summary(),
+        }), flush=True)
+
+
 # ------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     if rank != 0:
@@ -419,6 +560,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=["lloyd", "assign"], default="lloyd")
+    ap.add_argument("--stream", action="store_true",
+                    help="cfg5: stream x from host every iteration even when it fits in HBM")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -437,7 +580,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        (run_assign if args.op == "assign" else run_ours)(args, rank, world, local_rank)
+        if WORKLOADS[args.workload].get("large"):
+            run_large(args, rank, world, local_rank)
+        else:
+            (run_assign if args.op == "assign" else run_ours)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

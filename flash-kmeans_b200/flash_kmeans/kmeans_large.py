@@ -14,6 +14,11 @@ B200 design:
 * per device a copy stream and a compute stream over two block buffers; the
   copy of block i+1 (and of the next iteration's first blocks) overlaps the
   assignment of block i, ordered by events only (no host waits);
+* when a device's slice of x fits in half of its free HBM (a B200 holds
+  180 GB) and several passes are coming, the blocks are copied once into a
+  resident buffer during the first pass and later passes read them from
+  HBM: iterations stop being bound by the host link (all GPUs of a node
+  share the host's PCIe bandwidth);
 * x_sq per block is computed once and kept on the device;
 * each block goes through fk_assign_accumulate: labels, counts and per-cluster
   row sums in one call (one kernel for 16-bit data with D <= 128);
@@ -58,21 +63,39 @@ def partition_blocks(N: int, BLOCK_N: int, G: int):
     return blocks_per_gpu, point_start, point_end
 
 
-class _DeviceLane:
-    """Per-device streaming pipeline for one contiguous slice of x."""
+def _fits_resident(dev, rows: int, D: int, dtype: torch.dtype) -> bool:
+    """Whether `rows` rows of x (padded like the block buffers) take at most
+    half of the device's free memory."""
+    esize = torch.empty((), dtype=dtype).element_size()
+    row_bytes = -(-D * esize // 16) * 16
+    free, _ = torch.cuda.mem_get_info(dev)
+    return rows * row_bytes <= free // 2
 
-    def __init__(self, dev, x_host, p0, p1, BLOCK_N, K, D, dtype):
+
+class _DeviceLane:
+    """Per-device streaming pipeline for one contiguous slice of x.
+
+    ``resident``: copy every block once into one device buffer and reuse it
+    on later passes (no per-pass host transfers)."""
+
+    def __init__(self, dev, x_host, p0, p1, BLOCK_N, K, D, dtype, resident: bool = False):
         self.dev = dev
         self.x_host = x_host
         self.p0, self.p1 = p0, p1
         self.BLOCK_N = BLOCK_N
         self.blocks = [(n0, min(n0 + BLOCK_N, p1)) for n0 in range(p0, p1, BLOCK_N)]
         self.K, self.D, self.dtype = K, D, dtype
+        self.resident = resident
         with torch.cuda.device(dev):
             self.copy_stream = torch.cuda.Stream(device=dev)
             self.compute_stream = torch.cuda.Stream(device=dev)
             nb = min(BLOCK_N, p1 - p0)
-            self.xbuf = [_ops.empty_rows(1, nb, D, dtype, dev) for _ in range(2)]
+            if resident:
+                # one buffer for the whole slice; block i is rows n0-p0 .. n1-p0
+                self.xres = _ops.empty_rows(1, p1 - p0, D, dtype, dev)
+                self.res_loaded = [torch.cuda.Event() for _ in self.blocks]
+                self.res_issued = False
+            self.xbuf = [_ops.empty_rows(1, nb, D, dtype, dev) for _ in range(1 if resident else 2)]
             self.stage = None
             if x_host.dtype != dtype or not (x_host.is_contiguous() and self.xbuf[0].is_contiguous()):
                 self.stage = [torch.empty((nb, D), dtype=x_host.dtype, device=dev) for _ in range(2)]
@@ -129,6 +152,26 @@ class _DeviceLane:
         while len(self._ahead) < 2 and self._issued < limit:
             self._prefetch_one()
 
+    def _load_resident(self) -> None:
+        """First pass of a resident lane: queue every block's copy into its
+        own rows of the resident buffer (no slot reuse, so no waits)."""
+        if self.res_issued:
+            return
+        self.res_issued = True
+        cs = self.copy_stream
+        with torch.cuda.device(self.dev), torch.cuda.stream(cs):
+            for i, (n0, n1) in enumerate(self.blocks):
+                nb = n1 - n0
+                dst = self.xres[0, n0 - self.p0:n1 - self.p0]
+                src = self.x_host[n0:n1]
+                if self.stage is None:
+                    dst.copy_(src, non_blocking=True)
+                else:
+                    st = self.stage[0][:nb]
+                    st.copy_(src, non_blocking=True)
+                    dst.copy_(st)
+                self.res_loaded[i].record(cs)
+
     # -------------------------------------------------------------- compute
     def run_pass(self, assign_only: bool = False, wrap: bool = False) -> None:
         """Assign (and accumulate) every block of this lane once.  With `wrap`
@@ -142,13 +185,22 @@ class _DeviceLane:
                 self.cnt.zero_()
             s = nat.stream_handle(self.dev)
             status = nat.ptr(self.stat[1:2])
-            self._refill(wrap)
+            if self.resident:
+                self._load_resident()
+            else:
+                self._refill(wrap)
             for i, (n0, n1) in enumerate(self.blocks):
-                blk, slot = self._ahead.pop(0)
-                assert blk == i, (blk, i)
                 nb = n1 - n0
-                ks.wait_event(self.loaded[slot])
-                xb = self.xbuf[slot][:, :nb]
+                if self.resident:
+                    slot = None
+                    if self._pass == 0:
+                        ks.wait_event(self.res_loaded[i])
+                    xb = self.xres[:, n0 - self.p0:n1 - self.p0]
+                else:
+                    blk, slot = self._ahead.pop(0)
+                    assert blk == i, (blk, i)
+                    ks.wait_event(self.loaded[slot])
+                    xb = self.xbuf[slot][:, :nb]
                 if self.xsq[i] is None:
                     self.xsq[i] = _ops.row_sqnorm(xb)
                 xsq = self.xsq[i]
@@ -166,8 +218,9 @@ class _DeviceLane:
                     nat.check(lib.fk_assign_accumulate(*args, nat.ptr(self.cnt), nat.ptr(self.sums),
                                                        nat.dtype_code(xb.dtype), *tail),
                               "fk_assign_accumulate")
-                self.free[slot].record(ks)
-                self._refill(wrap)
+                if not self.resident:
+                    self.free[slot].record(ks)
+                    self._refill(wrap)
             self._pass += 1
 
     def finalize(self) -> None:
@@ -278,7 +331,9 @@ def kmeans_largeN(
     K = int(n_clusters)
     blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
     active = [g for g in range(G) if blocks_per_gpu[g] > 0]
-    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype)
+    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype,
+                         resident=max_iters > 1 and _fits_resident(
+                             devices[g], point_end[g] - point_start[g], D, dtype))
              for g in active]
     primary = lanes[0]
 
