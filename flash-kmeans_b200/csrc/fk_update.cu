@@ -540,14 +540,41 @@ constexpr int kPrivChunk = 2048;
 constexpr size_t kPrivMaxSmem = 200 * 1024;
 static_assert(kPrivChunk % kPrivThreads == 0, "chunk must be a multiple of the block");
 
+// Per-warp staging of the privatised sum: two 2 KB buffers of rows.
+constexpr int kPrivStageBuf = 2048;
+constexpr size_t kPrivStageBytes = static_cast<size_t>(kPrivThreads / 32) * 2 * kPrivStageBuf;
+
 static int64_t priv_row(int64_t D) { return (D + 127) / 128 * 128; }
 
 static size_t priv_smem_bytes(int64_t K, int64_t D) {
   return static_cast<size_t>(K * priv_row(D) + 3 * K + 3 * kPrivChunk + 4) * 4;
 }
 
+// Whether the staged (cp.async) variant applies: rows of D * esize bytes, a
+// power of two between 64 bytes and one 2 KB buffer, 16-byte aligned, and
+// room for the staging buffers next to the private sums.
+static bool priv_staged(int64_t K, int64_t D, int64_t row_bytes, bool aligned) {
+  return aligned && row_bytes >= 64 && row_bytes <= kPrivStageBuf &&
+         (row_bytes & (row_bytes - 1)) == 0 &&
+         align_up(priv_smem_bytes(K, D), 16) + kPrivStageBytes <= kPrivMaxSmem;
+}
+
 bool segsum_priv_fits(int64_t K, int64_t D) {
   return D <= 512 && priv_smem_bytes(K, D) <= kPrivMaxSmem;
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only), and its group
+// bookkeeping: a warp keeps one batch of rows in flight while it sums the
+// previous one, without holding the rows in registers.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Four consecutive columns d..d+3 of a row as float (missing ones 0).
@@ -570,8 +597,9 @@ __device__ __forceinline__ void load4_f(const T* row, int d, int D, int64_t sxd,
   }
 }
 
-// NG = number of 128-column groups of a row (1, 2 or 4).
-template <typename T, typename I, int NG>
+// NG = number of 128-column groups of a row (1, 2 or 4); STAGED: rows reach
+// shared memory through per-warp cp.async batches (see priv_staged).
+template <typename T, typename I, int NG, bool STAGED>
 __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
     const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd, const I* __restrict__ ids,
     int64_t sib, int64_t sin, int N, int K, int D, int64_t total, float* __restrict__ sums,
@@ -586,6 +614,8 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
   int* sslot = slab + kPrivChunk;                                         // [chunk] slot in bin
   int* perm = sslot + kPrivChunk;                                         // [chunk] sorted
   int* s_nvalid = perm + kPrivChunk;
+  uint8_t* wstage = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(s_nvalid + 1) + 15) & ~static_cast<uintptr_t>(15));
   const int64_t begin = static_cast<int64_t>(blockIdx.x) * total / gridDim.x;
   const int64_t end = static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -685,6 +715,55 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
             }
           }
       };
+      if constexpr (STAGED) {
+        // batches of RB rows (one 2 KB buffer) in sorted order; batch b+1's
+        // copies are in flight while batch b is summed from shared memory
+        const int rowb = D * static_cast<int>(sizeof(T));
+        const int RB = kPrivStageBuf / rowb;
+        uint8_t* wst = wstage + static_cast<size_t>(warp) * 2 * kPrivStageBuf;
+        auto issue = [&](int qb, int buf) {
+#pragma unroll
+          for (int i = 0; i < kPrivStageBuf / 512; ++i) {
+            const int byte = i * 512 + lane * 16;
+            const int q = qb + byte / rowb;
+            if (q < q1) {
+              const int j = perm[q];
+              cp_async16(wst + buf * kPrivStageBuf + byte,
+                         reinterpret_cast<const uint8_t*>(xb + (n0 + j) * sxn) + (byte % rowb));
+            }
+          }
+          cp_async_commit();
+        };
+        if (q0 < q1) issue(q0, 0);
+        int buf = 0;
+        for (int qb = q0; qb < q1; qb += RB, buf ^= 1) {
+          if (qb + RB < q1) issue(qb + RB, buf ^ 1);
+          else cp_async_commit();  // keep one group per step
+          cp_async_wait<1>();      // batch qb has landed (this lane's copies)
+          __syncwarp();            // ... and every lane's
+          const uint8_t* rows = wst + buf * kPrivStageBuf;
+          for (int rr = 0; rr < RB && qb + rr < q1; ++rr) {
+            const int lab = slab[perm[qb + rr]];
+            if (lab != cur) {
+              if (cur >= 0) flush();
+              cur = lab;
+            }
+            const T* row = reinterpret_cast<const T*>(rows + rr * rowb);
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+              const int d = g * 128 + lane * 4;
+              if (d < D) {
+                float f[4];
+                load4_f<T>(row, d, D, 1, true, f);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[g][e] += f[e];
+              }
+            }
+          }
+          __syncwarp();  // the buffer is refilled two steps later
+        }
+        cp_async_wait<0>();
+      } else {
       // rows loaded per warp before summing (more would lower occupancy)
       constexpr int kB = 4;
       for (int q = q0; q < q1; q += kB) {
@@ -719,6 +798,7 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
             }
         }
       }
+      }
       if (cur >= 0) flush();
       __syncthreads();
     }
@@ -751,12 +831,13 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
   }
 }
 
-template <typename T, typename I, int NG>
+template <typename T, typename I, int NG, bool STAGED>
 static int launch_priv_ng(const void* x, const int64_t* xs, const void* ids, const int64_t* is,
                           int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
                           int32_t* counts, int32_t* status, cudaStream_t s) {
-  const size_t smem = priv_smem_bytes(K, D);
-  auto kern = segsum_priv_kernel<T, I, NG>;
+  const size_t smem = STAGED ? align_up(priv_smem_bytes(K, D), 16) + kPrivStageBytes + 16
+                             : priv_smem_bytes(K, D);
+  auto kern = segsum_priv_kernel<T, I, NG, STAGED>;
   static bool attr_done[64] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "segsum_priv: no current device");
@@ -792,9 +873,17 @@ template <typename T, typename I>
 static int launch_priv_typed(const void* x, const int64_t* xs, const void* ids, const int64_t* is,
                              int64_t B, int64_t N, int64_t K, int64_t D, float* sums,
                              int32_t* counts, int32_t* status, cudaStream_t s) {
-  if (D <= 128) return launch_priv_ng<T, I, 1>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
-  if (D <= 256) return launch_priv_ng<T, I, 2>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
-  return launch_priv_ng<T, I, 4>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  const int64_t eb = sizeof(T);
+  const bool aligned = xs[2] == 1 && D % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                       (xs[1] * eb) % 16 == 0 && (B == 1 || (xs[0] * eb) % 16 == 0);
+  if (priv_staged(K, D, D * eb, aligned)) {
+    if (D <= 128) return launch_priv_ng<T, I, 1, true>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+    if (D <= 256) return launch_priv_ng<T, I, 2, true>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+    return launch_priv_ng<T, I, 4, true>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  }
+  if (D <= 128) return launch_priv_ng<T, I, 1, false>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  if (D <= 256) return launch_priv_ng<T, I, 2, false>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
+  return launch_priv_ng<T, I, 4, false>(x, xs, ids, is, B, N, K, D, sums, counts, status, s);
 }
 
 int segsum_priv(const void* x, int dtype, const int64_t* xs, const void* ids, int ids_dtype,
