@@ -41,20 +41,24 @@
 namespace fk {
 
 constexpr int kRows = 128;            // points per tile (MMA M)
-constexpr int kCent = 256;            // centroids per tile (MMA N)
-constexpr int kAcc = 2;               // TMEM accumulators (kAcc x kCent = all 512 columns)
+constexpr int kCent = 256;            // centroids per tile (MMA N); 128 for K <= 128
+constexpr int kTmemCols = 512;        // accumulators: kTmemCols / tile width of them
 constexpr int kChunkB = 128;          // bytes per row chunk = one 128B swizzle span
 constexpr int kXChunk = kRows * kChunkB;   // 16 KB
-constexpr int kCChunk = kCent * kChunkB;   // 32 KB
 constexpr int kEpiWarp0 = 2;           // epilogue warps start here (EPI of them)
 constexpr int kConvWarps = 4;          // fp32 split warps / sum warps after the epilogue
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
 
-template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8>
+template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8, int KC = kCent>
 struct Layout {
-  static constexpr int kGroups = EPI / 4;  // column groups of each 256-centroid tile
+  static constexpr int kGroups = EPI / 4;  // column groups of each centroid tile
   static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
-  static constexpr int XB = FUSE ? 3 : 2;              // resident x tile buffers
+  static constexpr int kCChunk = KC * kChunkB;        // one 128-byte column chunk of a tile
+  static constexpr int kAcc = kTmemCols / KC;          // TMEM accumulators
+  // resident x tile buffers: a third one lets the fused sum warps hold a tile,
+  // or (narrow tiles, one centroid tile per point tile) lets x loads run
+  // further ahead of the short per-tile MMA work
+  static constexpr int XB = (FUSE || KC < kCent) ? 3 : 2;
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -312,11 +316,14 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
 };
 
 // --------------------------------------------------------------------- kernel
-template <typename T, int MODE, bool XRES, int STAGES, bool FUSE, int EPI>
-__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI>::threads, 1)
+template <typename T, int MODE, bool XRES, int STAGES, bool FUSE, int EPI, int KC>
+__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::threads, 1)
     assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
-  using L = Layout<MODE, XRES, STAGES, FUSE, EPI>;
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC>;
+  constexpr int kCent = KC;                 // this instance's tile width
+  constexpr int kAcc = L::kAcc;
+  constexpr int kCChunk = L::kCChunk;
   constexpr int kEpiWarps = EPI;
   constexpr int kGroups = L::kGroups;
   constexpr int kGCols = kCent / kGroups;   // columns per group
@@ -782,14 +789,15 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI>::threads
 }
 
 // ------------------------------------------------------------------ host side
-template <typename T, int MODE, bool XRES, bool FUSE = false>
+template <typename T, int MODE, bool XRES, bool FUSE = false, int KC = kCent>
 static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
                          cudaStream_t stream) {
-  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : 4);  // centroid ring depth
+  // centroid ring depth (the narrow-tile ring holds as many bytes in twice the stages)
+  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4));
   constexpr int EPI = 8;  // epilogue warps: 4 TMEM lane quarters x 2 column halves
-  using L = Layout<MODE, XRES, STAGES, FUSE, EPI>;
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC>;
   static_assert(L::total <= 232448, "shared memory budget");
-  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI>;
+  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI, KC>;
   const int dev = current_device();
   static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);
@@ -871,9 +879,13 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   const int mode = is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2;
   const int dch = kChunkB / eb;
   const int nd = static_cast<int>((D + dch - 1) / dch);
-  const int nkt = static_cast<int>((K + kCent - 1) / kCent);
-  const int64_t kpad = static_cast<int64_t>(nkt) * kCent;
   const bool xres = is16 && nd <= kResidentChunks;
+  // K <= 128 (one centroid tile either way): 128-column tiles, so the epilogue
+  // skips the padding half of a 256-column tile and TMEM holds four accumulators
+  const bool narrow = is16 && !sums && K <= kCent / 2;
+  const int kc = narrow ? kCent / 2 : kCent;
+  const int nkt = static_cast<int>((K + kc - 1) / kc);
+  const int64_t kpad = static_cast<int64_t>(nkt) * kc;
 
   // 1) padded c_sq in the distance dtype
   if (c_sq) {
@@ -912,7 +924,7 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   CUtensorMap tx, tc;
   int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows);
   if (st != FK_OK) return st;
-  st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kCent);
+  st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc);
   if (st != FK_OK) return st;
 
   AssignParams p;
@@ -943,6 +955,12 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
       if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
       return mode == 0 ? launch_assign<T, 0, true, true>(tx, tc, p, stream)
                        : launch_assign<T, 1, true, true>(tx, tc, p, stream);
+    }
+    if (narrow) {
+      if (mode == 0) return xres ? launch_assign<T, 0, true, false, kCent / 2>(tx, tc, p, stream)
+                                 : launch_assign<T, 0, false, false, kCent / 2>(tx, tc, p, stream);
+      return xres ? launch_assign<T, 1, true, false, kCent / 2>(tx, tc, p, stream)
+                  : launch_assign<T, 1, false, false, kCent / 2>(tx, tc, p, stream);
     }
     if (mode == 0) return xres ? launch_assign<T, 0, true>(tx, tc, p, stream)
                                : launch_assign<T, 0, false>(tx, tc, p, stream);
