@@ -1,7 +1,7 @@
 """Benchmark of the Lloyd-iteration hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg1|cfg3|cfg4] [--op lloyd|assign]
+                    [--workload cfg2|cfg1|cfg3|cfg4|cfg5] [--op lloyd|assign] [--stream]
 
 A step is one Lloyd iteration (assign + update + shift check) over the whole
 batch of the workload.  Default workload: BASELINE config 2 (B=32, N=75600,
@@ -20,6 +20,11 @@ reference's torch path) on a bounded sample, all host cores via a spawn pool.
 Python/Triton package; its CPU path is restated in oracle/).
 `--op assign`: the assignment alone (`euclid_assign_triton`, labels only, the
 predict path) per step, instead of a Lloyd iteration.
+`--workload cfg5`: BASELINE config 5, out-of-core `kmeans_largeN` (N=2^26,
+D=128, K=8192, fp32) with x in pinned host memory, N partitioned over the
+ranks (strong scaling, NCCL all-reduce of the partial sums); each rank's shard
+stays resident in HBM after the first pass when it fits, `--stream` re-streams
+it every iteration instead.
 """
 from __future__ import annotations
 

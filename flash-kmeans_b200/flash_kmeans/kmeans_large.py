@@ -296,6 +296,7 @@ def kmeans_largeN(
     dtype: Optional[torch.dtype] = None,
     *,
     process_group=None,
+    resident: Optional[bool] = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Lloyd k-means for x (N, D) in host memory, streamed in blocks of BLOCK_N.
 
@@ -303,7 +304,11 @@ def kmeans_largeN(
     a device pins the run to that GPU.  ``process_group`` (extension): x is
     this process's contiguous shard, the process drives one GPU (``device``
     or the current one) and partial sums are all-reduced over the group;
-    labels of the shard are returned on the device.
+    labels of the shard are returned on the device.  ``resident``
+    (extension): None keeps a device's slice of x in HBM after the first pass
+    when it takes at most half of the free device memory and ``max_iters`` >
+    1; False streams every pass like the reference; True keeps it resident
+    regardless (the allocation must succeed).
 
     Returns (cluster_ids int32 (N,), centroids (K, D)).
     """
@@ -331,9 +336,13 @@ def kmeans_largeN(
     K = int(n_clusters)
     blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
     active = [g for g in range(G) if blocks_per_gpu[g] > 0]
+    def keep(g):
+        if resident is not None:
+            return bool(resident)
+        return max_iters > 1 and _fits_resident(devices[g], point_end[g] - point_start[g], D, dtype)
+
     lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype,
-                         resident=max_iters > 1 and _fits_resident(
-                             devices[g], point_end[g] - point_start[g], D, dtype))
+                         resident=keep(g))
              for g in active]
     primary = lanes[0]
 

@@ -181,19 +181,17 @@ def test_kmeans_largeN_single_gpu_vs_oracle(fk):
     assert torch.equal(lab2, direct)
 
 
-def test_kmeans_largeN_streaming_equals_resident(fk, monkeypatch):
-    """Slices that fit in HBM are copied once and kept resident; the streaming
-    pipeline (double-buffered blocks, next pass prefetched) gives the same run."""
-    from flash_kmeans import kmeans_large as kl
+def test_kmeans_largeN_streaming_equals_resident(fk):
+    """Slices that fit in HBM are copied once and kept resident (the default here); the
+    streaming pipeline (double-buffered blocks, next pass prefetched) gives the same run."""
     rng = np.random.default_rng(12)
     x = ko.gmm_points(rng, 1, 200_000, 24, 16, 5.0)[0]
     c0 = torch.from_numpy(x[rng.integers(0, len(x), 16)])
     xt = torch.from_numpy(x).pin_memory()
     lab_r, cent_r = fk.kmeans_largeN(xt, 16, max_iters=5, tol=-1, BLOCK_N=30_000,
                                      init_centroids=c0, device="cuda:0")
-    monkeypatch.setattr(kl, "_fits_resident", lambda *a, **k: False)
     lab_s, cent_s = fk.kmeans_largeN(xt, 16, max_iters=5, tol=-1, BLOCK_N=30_000,
-                                     init_centroids=c0, device="cuda:0")
+                                     init_centroids=c0, device="cuda:0", resident=False)
     # float32 atomics sum in a different order run to run, so a few near-tie points may
     # move over 5 free-running iterations: the north star's label / centroid bar
     assert (lab_r == lab_s).double().mean().item() >= 0.999
