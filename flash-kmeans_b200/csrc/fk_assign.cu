@@ -49,7 +49,8 @@ constexpr int kEpiWarp0 = 2;           // epilogue warps start here (EPI of them
 constexpr int kConvWarps = 4;          // fp32 split warps / sum warps after the epilogue
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
 
-template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8, int KC = kCent>
+template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8, int KC = kCent,
+          bool RESC = false>
 struct Layout {
   static constexpr int kGroups = EPI / 4;  // column groups of each centroid tile
   static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
@@ -57,8 +58,9 @@ struct Layout {
   static constexpr int kAcc = kTmemCols / KC;          // TMEM accumulators
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
   // or (narrow tiles, one centroid tile per point tile) lets x loads run
-  // further ahead of the short per-tile MMA work
-  static constexpr int XB = (FUSE || KC < kCent) ? 3 : 2;
+  // further ahead of the short per-tile MMA work; with resident centroids
+  // (RESC) the ring is small and five x tiles fit
+  static constexpr int XB = RESC ? 5 : ((FUSE || KC < kCent) ? 3 : 2);
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -78,9 +80,9 @@ struct Layout {
   static constexpr int save_off = lab_off + lab_bytes;
   static constexpr int save_bytes = (MODE == 0) ? 4 * save_stride * 16 : 0;
   static constexpr int bar_off = save_off + save_bytes;
-  // x_full[3] x_empty[3] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
+  // x_full[XB] x_empty[XB] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
-  static constexpr int nbars = 6 + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
+  static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
   static constexpr int threads = (kEpiWarp0 + EPI + ((MODE == 2 || FUSE) ? kConvWarps : 0)) * 32;
@@ -316,11 +318,17 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
 };
 
 // --------------------------------------------------------------------- kernel
-template <typename T, int MODE, bool XRES, int STAGES, bool FUSE, int EPI, int KC>
-__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::threads, 1)
+// RESC (resident centroids; 16-bit, resident x, nkt * nd <= STAGES): stage
+// s = kt * nd + dc holds that chunk of the current batch's centroids.  The
+// producer loads the chunks only when a CTA's tile range enters a new batch
+// (batch bi of the CTA: fill bi of every stage); the MMA waits for them once
+// per batch and releases them after the batch's last tile.
+template <typename T, int MODE, bool XRES, int STAGES, bool FUSE, int EPI, int KC, bool RESC>
+__global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>::threads, 1)
     assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
-  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC>;
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
+  static_assert(!RESC || (XRES && MODE != 2), "resident centroids need resident x, 16-bit");
   constexpr int kCent = KC;                 // this instance's tile width
   constexpr int kAcc = L::kAcc;
   constexpr int kCChunk = L::kCChunk;
@@ -344,8 +352,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar_off);
   uint64_t* x_full = bars;
-  uint64_t* x_empty = bars + 3;
-  uint64_t* c_full = bars + 6;
+  uint64_t* x_empty = bars + L::XB;
+  uint64_t* c_full = bars + 2 * L::XB;
   uint64_t* c_empty = c_full + STAGES;
   uint64_t* conv_full = c_empty + STAGES;
   uint64_t* acc_full = conv_full + STAGES;
@@ -359,7 +367,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < L::XB; ++i) {
       mbar_init(&x_full[i], 1);
       // with FUSE the resident x tile is also read by the 128 sum threads
       // (the points' rows) before it may be overwritten
@@ -406,7 +414,9 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
       uint32_t xph = 0;
       int last_par[STAGES];
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
-      int last_xpar[3] = {-1, -1, -1};
+      int last_xpar[L::XB];
+      for (int i = 0; i < L::XB; ++i) last_xpar[i] = -1;
+      int bi = -1, prev_b = -1;  // RESC: batch count of this CTA, last batch loaded
       bool ok = true;
       for (int t = t_begin; ok && t < t_end; ++t) {
         const int b = t / p.ntn;
@@ -423,19 +433,40 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
           last_xpar[xb] = static_cast<int>(xph);
           if (++xb == L::XB) { xb = 0; xph ^= 1; }
         }
-        for (int kt = 0; ok && kt < p.nkt; ++kt) {
-          for (int dc = 0; dc < p.nd; ++dc) {
-            if (!mbar_wait(&c_empty[stage], sph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
-              ok = false;
-              break;
+        if constexpr (RESC) {
+          if (b != prev_b) {
+            ++bi;
+            prev_b = b;
+            for (int kt = 0; ok && kt < p.nkt; ++kt)
+              for (int dc = 0; ok && dc < p.nd; ++dc) {
+                const int sc = kt * p.nd + dc;
+                // the previous batch's chunk is released after its last tile
+                if (!mbar_wait(&c_empty[sc], static_cast<uint32_t>(bi & 1) ^ 1u, abort_flag,
+                               p.status, FK_DEV_WAIT_TIMEOUT)) {
+                  ok = false;
+                  break;
+                }
+                mbar_arrive_expect_tx(&c_full[sc], kCChunk);
+                tma_load_3d(smem + L::stages_off + sc * L::stage_bytes + L::st_c, &tmap_c,
+                            &c_full[sc], dc * p.dch, kt * kCent, b);
+                last_par[sc] = bi & 1;
+              }
+          }
+        } else {
+          for (int kt = 0; ok && kt < p.nkt; ++kt) {
+            for (int dc = 0; dc < p.nd; ++dc) {
+              if (!mbar_wait(&c_empty[stage], sph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+                ok = false;
+                break;
+              }
+              uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
+              mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : kXChunk));
+              tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
+              if constexpr (!XRES)
+                tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
+              last_par[stage] = static_cast<int>(sph);
+              if (++stage == STAGES) { stage = 0; sph ^= 1; }
             }
-            uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
-            mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : kXChunk));
-            tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
-            if constexpr (!XRES)
-              tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
-            last_par[stage] = static_cast<int>(sph);
-            if (++stage == STAGES) { stage = 0; sph ^= 1; }
           }
         }
       }
@@ -457,8 +488,19 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
       uint32_t xph = 0;
       int ab = 0;
       uint32_t aph = 0;
+      int bi = -1, prev_b = -1;  // RESC: as in the producer
       bool ok = true;
       for (int t = t_begin; ok && t < t_end; ++t) {
+        bool new_batch = false, last_of_batch = false;
+        if constexpr (RESC) {
+          const int b = t / p.ntn;
+          new_batch = b != prev_b;
+          if (new_batch) {
+            ++bi;
+            prev_b = b;
+          }
+          last_of_batch = t + 1 == t_end || (t + 1) / p.ntn != b;
+        }
         if constexpr (XRES) {
           if (!mbar_wait(&x_full[xb], xph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
             ok = false;
@@ -474,13 +516,17 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
           for (int dc = 0; dc < p.nd; ++dc) {
-            uint64_t* ready = (MODE == 2) ? &conv_full[stage] : &c_full[stage];
-            if (!mbar_wait(ready, sph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
-              ok = false;
-              break;
+            const int sc = RESC ? kt * p.nd + dc : stage;
+            uint64_t* ready = (MODE == 2) ? &conv_full[sc] : &c_full[sc];
+            if (!RESC || new_batch) {
+              if (!mbar_wait(ready, RESC ? static_cast<uint32_t>(bi & 1) : sph, abort_flag,
+                             p.status, FK_DEV_WAIT_TIMEOUT)) {
+                ok = false;
+                break;
+              }
             }
             tc_fence_after();
-            uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
+            uint8_t* st = smem + L::stages_off + sc * L::stage_bytes;
             const uint32_t a_addr =
                 XRES ? smem_u32(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk)
                      : smem_u32(st + L::st_x);
@@ -503,8 +549,12 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
                         idesc, acc);
               }
             }
-            mma_commit(&c_empty[stage]);
-            if (++stage == STAGES) { stage = 0; sph ^= 1; }
+            if constexpr (RESC) {
+              if (last_of_batch) mma_commit(&c_empty[sc]);
+            } else {
+              mma_commit(&c_empty[stage]);
+              if (++stage == STAGES) { stage = 0; sph ^= 1; }
+            }
           }
           if (!ok) break;
           mma_commit(&acc_full[ab]);
@@ -789,15 +839,18 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC>::thr
 }
 
 // ------------------------------------------------------------------ host side
-template <typename T, int MODE, bool XRES, bool FUSE = false, int KC = kCent>
+template <typename T, int MODE, bool XRES, bool FUSE = false, int KC = kCent, bool RESC = false>
 static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
                          cudaStream_t stream) {
-  // centroid ring depth (the narrow-tile ring holds as many bytes in twice the stages)
-  constexpr int STAGES = (MODE == 2) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4));
+  // centroid ring depth (the narrow-tile ring holds as many bytes in twice the
+  // stages; resident centroids need one stage per chunk of the batch)
+  constexpr int STAGES = RESC ? kResidentChunks
+                              : ((MODE == 2) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4)));
   constexpr int EPI = 8;  // epilogue warps: 4 TMEM lane quarters x 2 column halves
-  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC>;
+  using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
   static_assert(L::total <= 232448, "shared memory budget");
-  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI, KC>;
+  if (RESC && p.nkt * p.nd > STAGES) return fail(FK_ERR_UNSUPPORTED, "resident centroids do not fit");
+  auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
   const int dev = current_device();
   static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);
@@ -956,10 +1009,10 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
       return mode == 0 ? launch_assign<T, 0, true, true>(tx, tc, p, stream)
                        : launch_assign<T, 1, true, true>(tx, tc, p, stream);
     }
-    if (narrow) {
-      if (mode == 0) return xres ? launch_assign<T, 0, true, false, kCent / 2>(tx, tc, p, stream)
+    if (narrow) {  // one centroid tile: resident in the stages when x is resident
+      if (mode == 0) return xres ? launch_assign<T, 0, true, false, kCent / 2, true>(tx, tc, p, stream)
                                  : launch_assign<T, 0, false, false, kCent / 2>(tx, tc, p, stream);
-      return xres ? launch_assign<T, 1, true, false, kCent / 2>(tx, tc, p, stream)
+      return xres ? launch_assign<T, 1, true, false, kCent / 2, true>(tx, tc, p, stream)
                   : launch_assign<T, 1, false, false, kCent / 2>(tx, tc, p, stream);
     }
     if (mode == 0) return xres ? launch_assign<T, 0, true>(tx, tc, p, stream)

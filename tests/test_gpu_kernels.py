@@ -99,6 +99,24 @@ def test_assign_shapes_vs_oracle(fk, dt, shape):
     assert_labels(x, c, ids, want, dt, f"{dt} {shape}")
 
 
+@pytest.mark.parametrize("dt,xsq_f32", [("float16", False), ("bfloat16", False), ("float16", True)])
+def test_assign_narrow_tiles_across_batches(fk, dt, xsq_f32):
+    """K <= 128: 128-column tiles with the batch's centroids resident in shared memory.
+    256 point tiles over the persistent CTAs, so many CTAs' tile ranges cross batches and
+    the centroids are reloaded mid-range."""
+    from flash_kmeans import _ops
+    from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+    B, N, K, D = 64, 500, 100, 128
+    rng = np.random.default_rng(17 + xsq_f32)
+    x = ko.round_to(rng.standard_normal((B, N, D), dtype=np.float32), dt)
+    c = ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt)
+    xd = _dev(x, dt)
+    xsq = (xd.float() ** 2).sum(-1) if xsq_f32 else _ops.row_sqnorm(xd)
+    ids = euclid_assign_triton(xd, _dev(c, dt), xsq).cpu().numpy()
+    want = ko.assign(x, c, _np(xsq), dt, xsq_dtype="float32" if xsq_f32 else None)
+    assert_labels(x, c, ids, want, dt, f"narrow {dt} xsq_f32={xsq_f32}")
+
+
 def test_assign_strided_inputs(fk):
     """Non-contiguous x (transposed storage) and a sliced batch go through packing."""
     from flash_kmeans.assign_euclid_triton import euclid_assign_triton
