@@ -136,9 +136,6 @@ struct Pack2<__half> {
   __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
     return __hlt2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   }
-  __device__ __forceinline__ static uint32_t ne_mask(uint32_t a, uint32_t b) {
-    return __hne2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
-  }
   __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
     const __half2 r = __hmin2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
     return *reinterpret_cast<const uint32_t*>(&r);
@@ -168,10 +165,6 @@ struct Pack2<__nv_bfloat16> {
   }
   __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
     return __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
-                       *reinterpret_cast<const __nv_bfloat162*>(&b));
-  }
-  __device__ __forceinline__ static uint32_t ne_mask(uint32_t a, uint32_t b) {
-    return __hne2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
                        *reinterpret_cast<const __nv_bfloat162*>(&b));
   }
   __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
