@@ -1111,6 +1111,11 @@ static bool assign_accumulate_fused(int64_t K, int64_t D, int dtype) {
   return nd <= kResidentChunks;
 }
 
+extern "C" int fk_assign_accumulate_method(int64_t K, int64_t D, int dtype) {
+  if (assign_accumulate_priv(K, D)) return FK_ACC_PRIVATISED;
+  return assign_accumulate_fused(K, D, dtype) ? FK_ACC_FUSED : FK_ACC_SORTED;
+}
+
 extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                       int dtype) {
   const size_t wa = fk_assign_workspace_size(B, K, dtype);

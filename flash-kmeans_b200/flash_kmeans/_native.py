@@ -16,6 +16,7 @@ LIB_NAME = "libflashkmeans_b200.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", LIB_NAME)
 
 FK_F16, FK_BF16, FK_F32, FK_I32, FK_I64 = 0, 1, 2, 3, 4
+FK_ACC_PRIVATISED, FK_ACC_FUSED, FK_ACC_SORTED = 0, 1, 2  # fk_assign_accumulate_method
 FK_OK = 0
 FK_DEV_BAD_LABEL = 101
 FK_DEV_WAIT_TIMEOUT = 102
@@ -47,6 +48,7 @@ SIGNATURES = {
     "fk_assign": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL, _PL, _PL,
                        _PL, _P, _S, _P, _P]),
     "fk_assign_accumulate_workspace_size": (_S, [_L, _L, _L, _L, _I]),
+    "fk_assign_accumulate_method": (_I, [_L, _L, _I]),
     "fk_assign_accumulate": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL,
                                   _PL, _PL, _PL, _P, _S, _P, _P]),
     "fk_assign_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL,

@@ -60,15 +60,12 @@ class LloydEngine:
     @property
     def kernels_per_step(self) -> int:
         """Kernel launches of one ``step()``, following fk_assign_accumulate's
-        choice: K x D float32 sums that fit in shared memory -> c_sq staging,
-        assignment, privatised sum, finalize; 16-bit rows of at most 128
-        elements -> c_sq staging, assignment with fused accumulation,
-        finalize; otherwise c_sq staging, assignment, scan, scatter,
-        segmented sum, finalize."""
-        if (self.K * self.D + self.K) * 4 <= 200 * 1024:
-            return 4
-        fused = self.dtype in (torch.float16, torch.bfloat16) and self.D <= 128
-        return 3 if fused else 6
+        method: privatised -> c_sq staging, assignment, privatised sum,
+        finalize; fused -> c_sq staging, assignment with fused accumulation,
+        finalize; sorted -> c_sq staging, assignment, scan, scatter, segmented
+        sum, finalize."""
+        method = nat.load().fk_assign_accumulate_method(self.K, self.D, nat.dtype_code(self.dtype))
+        return {nat.FK_ACC_PRIVATISED: 4, nat.FK_ACC_FUSED: 3}.get(method, 6)
 
     # ---------------------------------------------------------------- set-up
     def load(self, x: torch.Tensor, centroids: torch.Tensor, x_sq: torch.Tensor | None = None):

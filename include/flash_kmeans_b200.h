@@ -116,6 +116,13 @@ int fk_assign(const void* x, const void* centroids, const void* x_sq, const void
  * fk_centroid_accumulate; else with 16-bit x and D <= 128 it is one kernel
  * that reads x once; otherwise fk_assign then fk_centroid_accumulate. */
 size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
+
+/* How fk_assign_accumulate accumulates for these sizes (no counterpart in
+ * the reference, which always sorts): FK_ACC_PRIVATISED (a batch's K x D
+ * float32 sums fit in shared memory), FK_ACC_FUSED (16-bit x, D <= 128: one
+ * kernel), FK_ACC_SORTED (assignment, then counting sort + segmented sum). */
+enum fk_acc_method { FK_ACC_PRIVATISED = 0, FK_ACC_FUSED = 1, FK_ACC_SORTED = 2 };
+int fk_assign_accumulate_method(int64_t K, int64_t D, int dtype);
 int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
                          int32_t* out, int32_t* counts, float* sums, int dtype, int xsq_dtype,
                          int csq_dtype, int64_t B, int64_t N, int64_t K, int64_t D,

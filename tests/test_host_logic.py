@@ -108,3 +108,23 @@ def test_oracle_never_imported_by_package():
             "import flash_kmeans.kmeans_large, flash_kmeans.interface; "
             "assert not [m for m in sys.modules if m.startswith('oracle')]")
     subprocess.run([sys.executable, "-c", code], cwd=root, check=True)
+
+
+@pytest.mark.parametrize("K,D,dt", [(128, 128, 0), (380, 128, 0), (400, 128, 0), (1000, 128, 0),
+                                    (1000, 128, 1), (1000, 192, 0), (64, 32, 2), (8192, 128, 2),
+                                    (300, 100, 2), (100, 512, 0), (100, 600, 0)])
+def test_accumulate_method_matches_workspace(K, D, dt):
+    """fk_assign_accumulate_method is the choice fk_assign_accumulate makes: only the
+    sorted method needs workspace beyond the assignment's; the engine's launch count
+    follows it."""
+    from flash_kmeans import _native as nat
+    lib = nat.load()
+    m = lib.fk_assign_accumulate_method(K, D, dt)
+    assert m in (nat.FK_ACC_PRIVATISED, nat.FK_ACC_FUSED, nat.FK_ACC_SORTED)
+    extra = (lib.fk_assign_accumulate_workspace_size(2, 5000, K, D, dt)
+             - lib.fk_assign_workspace_size(2, K, dt))
+    assert (extra > 0) == (m == nat.FK_ACC_SORTED)
+    if m == nat.FK_ACC_FUSED:
+        assert dt in (0, 1) and D <= 128
+    if m == nat.FK_ACC_PRIVATISED:
+        assert K * D * 4 <= 200 * 1024
