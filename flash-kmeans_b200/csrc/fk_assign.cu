@@ -29,6 +29,12 @@
 //   2  float32 x: cross = 3xTF32 (hi*hi + hi*lo + lo*hi, hi = tf32-rounded
 //      value, lo = exact remainder, split in shared memory by the 4 extra warps),
 //      float32 chain.
+//   3  16-bit x, dot-product argmax (cosine / dot k-means, replaces
+//      _cosine_assign_kernel, assign_euclid_triton.py:1038-1131): the float32
+//      cross itself, maximised; run as the argmin of -cross + m, m = 0 for real
+//      centroids and +inf for padding columns (the c_sq slot), so padding never
+//      wins even when every real score is negative.
+//   4  float32 x, dot-product argmax with the 3xTF32 cross of mode 2.
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
 // centroid chunk instead of staying resident.
@@ -49,11 +55,14 @@ constexpr int kEpiWarp0 = 2;           // epilogue warps start here (EPI of them
 constexpr int kConvWarps = 4;          // fp32 split warps / sum warps after the epilogue
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
 
+// Modes 2 and 4 split float32 operands into tf32 hi/lo parts (converter warps).
+constexpr bool split_mode(int mode) { return mode == 2 || mode == 4; }
+
 template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8, int KC = kCent,
           bool RESC = false>
 struct Layout {
   static constexpr int kGroups = EPI / 4;  // column groups of each centroid tile
-  static constexpr int kSplit = (MODE == 2) ? 2 : 1;  // hi/lo copies for 3xTF32
+  static constexpr int kSplit = split_mode(MODE) ? 2 : 1;  // hi/lo copies for 3xTF32
   static constexpr int kCChunk = KC * kChunkB;        // one 128-byte column chunk of a tile
   static constexpr int kAcc = kTmemCols / KC;          // TMEM accumulators
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
@@ -85,7 +94,8 @@ struct Layout {
   static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
-  static constexpr int threads = (kEpiWarp0 + EPI + ((MODE == 2 || FUSE) ? kConvWarps : 0)) * 32;
+  static constexpr int threads =
+      (kEpiWarp0 + EPI + ((split_mode(MODE) || FUSE) ? kConvWarps : 0)) * 32;
 };
 
 struct AssignParams {
@@ -288,7 +298,8 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
       const int c = j % kChains;
       float cr = __uint_as_float(v[j]);
       if constexpr (MODE == 1) cr = round16<T>(cr);
-      const float d = __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
+      // modes 3/4: argmax of the score as argmin of -score (+inf on padding)
+      const float d = MODE >= 3 ? __fadd_rn(-cr, cs[j]) : __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
       const bool lt = d < best[c];
       best[c] = fminf(best[c], d);
       loc[c] = lt ? j : loc[c];
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     assign_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_c, const AssignParams p) {
   using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
-  static_assert(!RESC || (XRES && MODE != 2), "resident centroids need resident x, 16-bit");
+  static_assert(!RESC || (XRES && !split_mode(MODE)), "resident centroids need resident x, 16-bit");
   constexpr int kCent = KC;                 // this instance's tile width
   constexpr int kAcc = L::kAcc;
   constexpr int kCChunk = L::kCChunk;
@@ -510,7 +521,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
           for (int dc = 0; dc < p.nd; ++dc) {
             const int sc = RESC ? kt * p.nd + dc : stage;
-            uint64_t* ready = (MODE == 2) ? &conv_full[sc] : &c_full[sc];
+            uint64_t* ready = split_mode(MODE) ? &conv_full[sc] : &c_full[sc];
             if (!RESC || new_batch) {
               if (!mbar_wait(ready, RESC ? static_cast<uint32_t>(bi & 1) : sph, abort_flag,
                              p.status, FK_DEV_WAIT_TIMEOUT)) {
@@ -528,7 +539,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
             for (int ks = 0; ks < 4; ++ks) {
               const uint32_t acc = (dc > 0 || ks > 0) ? 1u : 0u;
               const uint32_t off = static_cast<uint32_t>(ks * 32);
-              if constexpr (MODE == 2) {
+              if constexpr (split_mode(MODE)) {
                 const uint32_t alo = smem_u32(st + L::st_xlo);
                 const uint32_t blo = smem_u32(st + L::st_clo);
                 mma_tf32(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off),
@@ -579,7 +590,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     // ahead so the tile's first distances do not wait on an HBM read
     auto load_xsq = [&](int t) -> float {
       const int n = (t % p.ntn) * kRows + row;
-      return n < p.N ? load_f(p.xsq, (t / p.ntn) * p.sxq_b + n * p.sxq_n, p.xsq_dtype) : 0.0f;
+      return (n < p.N && p.xsq) ? load_f(p.xsq, (t / p.ntn) * p.sxq_b + n * p.sxq_n, p.xsq_dtype)
+                                : 0.0f;
     };
     float xsq_next = t_begin < t_end ? load_xsq(t_begin) : 0.0f;
     for (int t = t_begin; ok && t < t_end; ++t, ++it) {
@@ -781,8 +793,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       if (++xi == L::XB) xi = 0;
     }
     }
-  } else if (MODE == 2) {
-    // ---------------------------------------- 3xTF32 split converters (mode 2)
+  } else if (split_mode(MODE)) {
+    // ------------------------------------- 3xTF32 split converters (modes 2, 4)
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
     int stage = 0;
     uint32_t sph = 0;
@@ -838,7 +850,7 @@ static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const Ass
   // centroid ring depth (the narrow-tile ring holds as many bytes in twice the
   // stages; resident centroids need one stage per chunk of the batch)
   constexpr int STAGES = RESC ? kResidentChunks
-                              : ((MODE == 2) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4)));
+                              : (split_mode(MODE) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4)));
   constexpr int EPI = 8;  // epilogue warps: 4 TMEM lane quarters x 2 column halves
   using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
   static_assert(L::total <= 232448, "shared memory budget");
@@ -914,27 +926,41 @@ __global__ void copy_csq_kernel(const void* __restrict__ csq_in, int csq_dtype, 
   }
 }
 
+// Dot-product modes: 0 for real centroids, +inf for the padding columns.
+__global__ void dot_mask_kernel(float* __restrict__ out, int64_t kpad, int K, int64_t total) {
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < total;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[r] = static_cast<int>(r % kpad) < K ? 0.0f : __int_as_float(0x7f800000);
+}
+
 template <typename T>
 static int assign_typed(const void* x, const void* cent, const void* x_sq, const void* c_sq,
                         int32_t* out, int32_t* counts, int xsq_dtype, int csq_dtype, int64_t B,
                         int64_t N, int64_t K, int64_t D, const int64_t* xs, const int64_t* cs,
                         const int64_t* xqs, const int64_t* cqs, const int64_t* os, void* ws,
-                        int32_t* status, cudaStream_t stream, float* sums = nullptr) {
+                        int32_t* status, cudaStream_t stream, float* sums = nullptr,
+                        bool dot = false) {
   constexpr int eb = Elem<T>::kBytes;
   const bool is16 = eb == 2;
-  const int mode = is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2;
+  const int mode = dot ? (is16 ? 3 : 4) : (is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2);
   const int dch = kChunkB / eb;
   const int nd = static_cast<int>((D + dch - 1) / dch);
   const bool xres = is16 && nd <= kResidentChunks;
   // K <= 128 (one centroid tile either way): 128-column tiles, so the epilogue
   // skips the padding half of a 256-column tile and TMEM holds four accumulators
-  const bool narrow = is16 && !sums && K <= kCent / 2;
+  const bool narrow = is16 && !sums && !dot && K <= kCent / 2;
   const int kc = narrow ? kCent / 2 : kCent;
   const int nkt = static_cast<int>((K + kc - 1) / kc);
   const int64_t kpad = static_cast<int64_t>(nkt) * kc;
 
-  // 1) padded c_sq in the distance dtype
-  if (c_sq) {
+  // 1) padded c_sq in the distance dtype (the 0 / +inf column mask for dot modes)
+  if (dot) {
+    const int64_t total = B * kpad;
+    const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    dot_mask_kernel<<<blocks, 256, 0, stream>>>(static_cast<float*>(ws), kpad, (int)K, total);
+    int st = check_launch("dot_mask_kernel");
+    if (st != FK_OK) return st;
+  } else if (c_sq) {
     const int64_t total = B * kpad;
     const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
     if (mode == 0)
@@ -975,8 +1001,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
 
   AssignParams p;
   p.xsq = x_sq;
-  p.sxq_b = xqs[0];
-  p.sxq_n = xqs[1];
+  p.sxq_b = xqs ? xqs[0] : 0;  // x_sq is not used by the dot-product modes
+  p.sxq_n = xqs ? xqs[1] : 0;
   p.xsq_dtype = xsq_dtype;
   p.csq = ws;
   p.kpad = kpad;
@@ -996,6 +1022,14 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.total_tiles = static_cast<int>(B * p.ntn);
   p.status = status;
 
+  if (dot) {
+    if (sums) return fail(FK_ERR_UNSUPPORTED, "fused sums are not built for dot-product modes");
+    if constexpr (Elem<T>::kBytes == 2)
+      return xres ? launch_assign<T, 3, true>(tx, tc, p, stream)
+                  : launch_assign<T, 3, false>(tx, tc, p, stream);
+    else
+      return launch_assign<T, 4, false>(tx, tc, p, stream);
+  }
   if constexpr (Elem<T>::kBytes == 2) {
     if (sums) {  // fused centroid sums: resident x tiles only (checked by the caller)
       if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
@@ -1028,29 +1062,31 @@ extern "C" size_t fk_assign_workspace_size(int64_t B, int64_t K, int dtype) {
   return align_up(static_cast<size_t>(B * kpad * 4), 256) + 256;
 }
 
-extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
-                         int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,
-                         int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
-                         const int64_t* c_strides3, const int64_t* xsq_strides2,
-                         const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
-                         size_t workspace_bytes, int32_t* dev_status, void* stream) {
+// fk_assign and fk_assign_dot: validation, TMA-friendly strides, dispatch.
+static int assign_entry(const char* fn, bool dot, const void* x, const void* centroids,
+                        const void* x_sq, const void* c_sq, int32_t* out, int32_t* counts,
+                        int dtype, int xsq_dtype, int csq_dtype, int64_t B, int64_t N, int64_t K,
+                        int64_t D, const int64_t* x_strides3, const int64_t* c_strides3,
+                        const int64_t* xsq_strides2, const int64_t* csq_strides2,
+                        const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
+                        int32_t* dev_status, void* stream) {
   if (B < 0 || N < 0 || K <= 0 || D <= 0)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign: bad sizes B=%lld N=%lld K=%lld D=%lld",
+    return fail(FK_ERR_INVALID_ARG, "%s: bad sizes B=%lld N=%lld K=%lld D=%lld", fn,
                 (long long)B, (long long)N, (long long)K, (long long)D);
   if (B == 0 || N == 0) return FK_OK;
-  if (!x || !centroids || !x_sq || !out || !x_strides3 || !c_strides3 || !xsq_strides2 ||
-      !out_strides2)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign: null pointer argument");
-  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "fk_assign: c_sq without strides");
+  if (!x || !centroids || (!dot && !x_sq) || !out || !x_strides3 || !c_strides3 ||
+      (!dot && !xsq_strides2) || !out_strides2)
+    return fail(FK_ERR_INVALID_ARG, "%s: null pointer argument", fn);
+  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "%s: c_sq without strides", fn);
   if (dtype != FK_F16 && dtype != FK_BF16 && dtype != FK_F32)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign: x dtype must be f16, bf16 or f32");
-  if (xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign: x_sq dtype must be floating");
+    return fail(FK_ERR_INVALID_ARG, "%s: x dtype must be f16, bf16 or f32", fn);
+  if (!dot && xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "%s: x_sq dtype must be floating", fn);
   if (c_sq && csq_dtype != FK_F16 && csq_dtype != FK_BF16 && csq_dtype != FK_F32)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign: c_sq dtype must be floating");
-  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "fk_assign: K=%lld above 2^20", (long long)K);
+    return fail(FK_ERR_INVALID_ARG, "%s: c_sq dtype must be floating", fn);
+  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "%s: K=%lld above 2^20", fn, (long long)K);
   if (N >= (1ll << 31) || B * ((N + kRows - 1) / kRows) >= (1ll << 31))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign: problem too large for 32-bit tile indices");
+    return fail(FK_ERR_UNSUPPORTED, "%s: problem too large for 32-bit tile indices", fn);
   // Strides of size-1 dimensions are irrelevant; give TMA valid ones.
   const int64_t eb = dtype == FK_F32 ? 4 : 2;
   const int64_t row_al = 16 / eb;
@@ -1063,28 +1099,49 @@ extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq,
   x_strides3 = xs;
   c_strides3 = cs;
   if (!fk_tma_compatible(x, dtype, D, x_strides3))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign: x rows not TMA-addressable (pack with fk_pack_rows)");
+    return fail(FK_ERR_UNSUPPORTED, "%s: x rows not TMA-addressable (pack with fk_pack_rows)", fn);
   if (!fk_tma_compatible(centroids, dtype, D, c_strides3))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign: centroid rows not TMA-addressable");
+    return fail(FK_ERR_UNSUPPORTED, "%s: centroid rows not TMA-addressable", fn);
   const size_t need = fk_assign_workspace_size(B, K, dtype);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
-    return fail(FK_ERR_WORKSPACE, "fk_assign: workspace needs %zu bytes, 256-aligned", need);
+    return fail(FK_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-aligned", fn, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case FK_F16:
       return assign_typed<__half>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N,
                                   K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
-                                  out_strides2, workspace, dev_status, s);
+                                  out_strides2, workspace, dev_status, s, nullptr, dot);
     case FK_BF16:
       return assign_typed<__nv_bfloat16>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype,
                                          csq_dtype, B, N, K, D, x_strides3, c_strides3,
                                          xsq_strides2, csq_strides2, out_strides2, workspace,
-                                         dev_status, s);
+                                         dev_status, s, nullptr, dot);
     default:
       return assign_typed<float>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N,
                                  K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
-                                 out_strides2, workspace, dev_status, s);
+                                 out_strides2, workspace, dev_status, s, nullptr, dot);
   }
+}
+
+extern "C" int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
+                         int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,
+                         int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
+                         const int64_t* c_strides3, const int64_t* xsq_strides2,
+                         const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
+                         size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  return assign_entry("fk_assign", false, x, centroids, x_sq, c_sq, out, counts, dtype, xsq_dtype,
+                      csq_dtype, B, N, K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
+                      out_strides2, workspace, workspace_bytes, dev_status, stream);
+}
+
+extern "C" int fk_assign_dot(const void* x, const void* centroids, int32_t* out, int32_t* counts,
+                             int dtype, int64_t B, int64_t N, int64_t K, int64_t D,
+                             const int64_t* x_strides3, const int64_t* c_strides3,
+                             const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
+                             int32_t* dev_status, void* stream) {
+  return assign_entry("fk_assign_dot", true, x, centroids, nullptr, nullptr, out, counts, dtype,
+                      FK_F32, FK_F32, B, N, K, D, x_strides3, c_strides3, nullptr, nullptr,
+                      out_strides2, workspace, workspace_bytes, dev_status, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -71,6 +71,34 @@ __global__ void row_sqnorm_vec_kernel(const T* __restrict__ x, int64_t sxb, int6
   }
 }
 
+// F.normalize(x, p=2, dim=-1) in x's dtype (kmeans_triton_impl.py:135): the
+// norm is accumulated in float32 and rounded to the dtype, clamped below by
+// eps = 1e-12 taken in the dtype (0 for float16), and each element is divided
+// in float32 and rounded.  One warp per row.
+template <typename T>
+__global__ void row_normalize_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn,
+                                     int64_t sxd, T* __restrict__ out, int64_t sob, int64_t son,
+                                     int64_t sod, int N, int D, int64_t rows) {
+  const int wpb = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const float eps = Elem<T>::round(1e-12f);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); r < rows;
+       r += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t b = r / N, n = r % N;
+    const T* row = x + b * sxb + n * sxn;
+    T* dst = out + b * sob + n * son;
+    float ss = 0.0f;
+    for (int d = lane; d < D; d += 32) {
+      const float e = Elem<T>::to_f(row[d * sxd]);
+      ss = __fmaf_rn(e, e, ss);
+    }
+    ss = warp_sum(ss);
+    const float den = fmaxf(Elem<T>::round(sqrtf(ss)), eps);
+    for (int d = lane; d < D; d += 32)
+      dst[d * sod] = Elem<T>::from_f(__fdiv_rn(Elem<T>::to_f(row[d * sxd]), den));
+  }
+}
+
 template <typename T>
 __global__ void pack_rows_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
                                  T* __restrict__ out, int N, int D, int Dp, int64_t total) {
@@ -168,6 +196,46 @@ extern "C" int fk_row_sqnorm(const void* x, int dtype, int64_t B, int64_t N, int
     default:
       return fail(FK_ERR_INVALID_ARG, "fk_row_sqnorm: unsupported dtype %d", dtype);
   }
+}
+
+extern "C" int fk_row_normalize(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                                const int64_t* x_strides3, void* out, const int64_t* out_strides3,
+                                void* stream) {
+  if (B < 0 || N < 0 || D <= 0) return fail(FK_ERR_INVALID_ARG, "fk_row_normalize: bad sizes");
+  if (B == 0 || N == 0) return FK_OK;
+  if (!x || !out || !x_strides3 || !out_strides3)
+    return fail(FK_ERR_INVALID_ARG, "fk_row_normalize: null pointer argument");
+  if (N >= (1ll << 31) || D >= (1ll << 31))
+    return fail(FK_ERR_UNSUPPORTED, "fk_row_normalize: N and D must be below 2^31");
+  const int64_t rows = B * N;
+  int64_t blocks = (rows + 7) / 8;
+  const int sms = sm_count_current();
+  const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 16 : 2048;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t* xs = x_strides3;
+  const int64_t* os = out_strides3;
+  switch (dtype) {
+    case FK_F16:
+      row_normalize_kernel<__half><<<static_cast<int>(blocks), 256, 0, s>>>(
+          static_cast<const __half*>(x), xs[0], xs[1], xs[2], static_cast<__half*>(out), os[0],
+          os[1], os[2], static_cast<int>(N), static_cast<int>(D), rows);
+      break;
+    case FK_BF16:
+      row_normalize_kernel<__nv_bfloat16><<<static_cast<int>(blocks), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), xs[0], xs[1], xs[2],
+          static_cast<__nv_bfloat16*>(out), os[0], os[1], os[2], static_cast<int>(N),
+          static_cast<int>(D), rows);
+      break;
+    case FK_F32:
+      row_normalize_kernel<float><<<static_cast<int>(blocks), 256, 0, s>>>(
+          static_cast<const float*>(x), xs[0], xs[1], xs[2], static_cast<float*>(out), os[0],
+          os[1], os[2], static_cast<int>(N), static_cast<int>(D), rows);
+      break;
+    default:
+      return fail(FK_ERR_INVALID_ARG, "fk_row_normalize: unsupported dtype %d", dtype);
+  }
+  return check_launch("row_normalize_kernel");
 }
 
 extern "C" int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,

@@ -483,6 +483,58 @@ __global__ void finalize_kernel(float* __restrict__ sums, int32_t* __restrict__ 
   }
 }
 
+// Cosine / dot-product finalize (_centroid_update_torch_native with
+// mode='cosine', torch_fallback.py:101-109): per (b, k) row the float32 mean
+// (the old centroid, as float32, when the cluster is empty) is L2-normalised
+// in float32 (F.normalize: / max(||m||, 1e-12)) and cast to the dtype; the
+// shift is round(||round(new - old)||) as for the Euclidean finalize.  Warp per
+// row, grid-stride.
+template <typename T>
+__global__ void finalize_normalized_kernel(const float* __restrict__ sums,
+                                           const int32_t* __restrict__ counts,
+                                           const T* __restrict__ old, int64_t sob, int64_t sok,
+                                           int64_t sod, T* __restrict__ out, int64_t snb,
+                                           int64_t snk, int64_t snd, int B, int K, int D,
+                                           float* __restrict__ shift_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wpb = blockDim.x >> 5;
+  float wmax = 0.f;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5);
+       r < static_cast<int64_t>(B) * K; r += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t b = r / K, k = r % K;
+    const int32_t cnt = counts[r];
+    const float fc = static_cast<float>(cnt);
+    const float* sm = sums + r * D;
+    const T* o = old + b * sob + k * sok;
+    T* nw = out + b * snb + k * snk;
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float m = cnt > 0 ? __fdiv_rn(sm[d], fc) : Elem<T>::to_f(o[d * sod]);
+      ss = __fmaf_rn(m, m, ss);
+    }
+    const float den = fmaxf(sqrtf(warp_sum(ss)), 1e-12f);
+    float ds = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float ov = Elem<T>::to_f(o[d * sod]);
+      const float m = cnt > 0 ? __fdiv_rn(sm[d], fc) : ov;
+      const float nv = Elem<T>::round(__fdiv_rn(m, den));
+      nw[d * snd] = Elem<T>::from_f(nv);
+      const float df = Elem<T>::round(nv - ov);
+      ds = __fmaf_rn(df, df, ds);
+    }
+    ds = warp_sum(ds);
+    if (lane == 0) wmax = fmaxf(wmax, Elem<T>::round(sqrtf(ds)));
+  }
+  __shared__ float blk_max[32];
+  if (lane == 0) blk_max[threadIdx.x >> 5] = wmax;
+  __syncthreads();
+  if (threadIdx.x == 0 && shift_out) {
+    float m = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, blk_max[w]);
+    atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(m));
+  }
+}
+
 static int grid_for(int64_t work, int per_block, int cap_per_sm) {
   int64_t blocks = (work + per_block - 1) / per_block;
   const int sms = sm_count_current();
@@ -1112,6 +1164,56 @@ extern "C" int fk_centroid_finalize(float* sums, int32_t* counts, const void* ol
   // the 4*B*K*D bytes at full bandwidth, while zero stores issued by the
   // finalize right behind its reads of the same (atomically updated) lines
   // tripled its time.
+  cudaError_t e = cudaMemsetAsync(sums, 0, static_cast<size_t>(rows * D) * sizeof(float), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, static_cast<size_t>(rows) * sizeof(int32_t), s);
+  if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return FK_OK;
+}
+
+extern "C" int fk_centroid_finalize_normalized(float* sums, int32_t* counts,
+                                               const void* old_centroids, void* new_centroids,
+                                               int dtype, int64_t B, int64_t K, int64_t D,
+                                               const int64_t* old_strides3,
+                                               const int64_t* new_strides3, float* shift_out,
+                                               int reset_accumulators, void* stream) {
+  if (B < 0 || K <= 0 || D <= 0)
+    return fail(FK_ERR_INVALID_ARG, "fk_centroid_finalize_normalized: bad sizes");
+  if (!sums || !counts || !old_centroids || !new_centroids || !old_strides3 || !new_strides3)
+    return fail(FK_ERR_INVALID_ARG, "fk_centroid_finalize_normalized: null pointer argument");
+  if (old_centroids == new_centroids)
+    return fail(FK_ERR_INVALID_ARG, "fk_centroid_finalize_normalized: new_centroids aliases old_centroids");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (shift_out) {
+    cudaError_t e = cudaMemsetAsync(shift_out, 0, sizeof(float), s);
+    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
+  if (B == 0) return FK_OK;
+  const int64_t rows = B * K;
+  const int grid = grid_for(rows, 8, 4);
+  const int64_t* os = old_strides3;
+  const int64_t* ns = new_strides3;
+  switch (dtype) {
+    case FK_F16:
+      finalize_normalized_kernel<__half><<<grid, 256, 0, s>>>(
+          sums, counts, static_cast<const __half*>(old_centroids), os[0], os[1], os[2],
+          static_cast<__half*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D, shift_out);
+      break;
+    case FK_BF16:
+      finalize_normalized_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          sums, counts, static_cast<const __nv_bfloat16*>(old_centroids), os[0], os[1], os[2],
+          static_cast<__nv_bfloat16*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D,
+          shift_out);
+      break;
+    case FK_F32:
+      finalize_normalized_kernel<float><<<grid, 256, 0, s>>>(
+          sums, counts, static_cast<const float*>(old_centroids), os[0], os[1], os[2],
+          static_cast<float*>(new_centroids), ns[0], ns[1], ns[2], (int)B, (int)K, (int)D, shift_out);
+      break;
+    default:
+      return fail(FK_ERR_INVALID_ARG, "fk_centroid_finalize_normalized: unsupported dtype %d", dtype);
+  }
+  int st = check_launch("finalize_normalized_kernel");
+  if (st != FK_OK || !reset_accumulators) return st;
   cudaError_t e = cudaMemsetAsync(sums, 0, static_cast<size_t>(rows * D) * sizeof(float), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, static_cast<size_t>(rows) * sizeof(int32_t), s);
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));

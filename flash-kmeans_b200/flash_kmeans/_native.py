@@ -43,10 +43,12 @@ SIGNATURES = {
     "fk_device_sm_count": (_I, []),
     "fk_tma_compatible": (_I, [_P, _I, _L, _PL]),
     "fk_row_sqnorm": (_I, [_P, _I, _L, _L, _L, _PL, _P, _I, _PL, _P]),
+    "fk_row_normalize": (_I, [_P, _I, _L, _L, _L, _PL, _P, _PL, _P]),
     "fk_pack_rows": (_I, [_P, _I, _L, _L, _L, _PL, _P, _L, _P]),
     "fk_assign_workspace_size": (_S, [_L, _L, _I]),
     "fk_assign": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL, _PL, _PL,
                        _PL, _P, _S, _P, _P]),
+    "fk_assign_dot": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _L, _PL, _PL, _PL, _P, _S, _P, _P]),
     "fk_assign_accumulate_workspace_size": (_S, [_L, _L, _L, _L, _I]),
     "fk_assign_accumulate_method": (_I, [_L, _L, _I]),
     "fk_assign_accumulate": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL,
@@ -57,6 +59,8 @@ SIGNATURES = {
     "fk_centroid_accumulate": (_I, [_P, _I, _L, _L, _L, _L, _PL, _P, _I, _PL, _P, _P, _P, _P,
                                     _S, _P, _P]),
     "fk_centroid_finalize": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _PL, _PL, _P, _P, _I, _P]),
+    "fk_centroid_finalize_normalized": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _PL, _PL, _P, _I,
+                                             _P]),
 }
 
 ABI_VERSION = 1

@@ -82,6 +82,20 @@ def row_sqnorm(x: torch.Tensor, out_dtype=None, out: torch.Tensor | None = None)
     return out
 
 
+def row_normalize(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """F.normalize(x, p=2, dim=-1) over (B, N, D) in x's dtype (kernel fk_row_normalize)."""
+    _require_cuda(x)
+    B, N, D = x.shape
+    if out is None:
+        out = empty_rows(B, N, D, x.dtype, x.device)
+    lib = nat.load()
+    with torch.cuda.device(x.device):
+        nat.check(lib.fk_row_normalize(nat.ptr(x), nat.dtype_code(x.dtype), B, N, D,
+                                       nat.strides(x, 3), nat.ptr(out), nat.strides(out, 3),
+                                       nat.stream_handle(x.device)), "fk_row_normalize")
+    return out
+
+
 class DeviceStatus:
     """Per-device int32 word that kernels set on asynchronous errors."""
 
@@ -161,3 +175,33 @@ def finalize(sums, counts, old, new, csq_out=None, shift_out=None, reset=False) 
             B, K, D, nat.strides(old, 3), nat.strides(new, 3), nat.ptr(csq_out),
             nat.ptr(shift_out), 1 if reset else 0, nat.stream_handle(old.device)),
             "fk_centroid_finalize")
+
+
+def assign_dot(x, centroids, out=None, counts=None, status=None) -> torch.Tensor:
+    """Launch fk_assign_dot (argmax of x.c).  x / centroids must be TMA-compatible."""
+    B, N, D = x.shape
+    K = centroids.shape[1]
+    if out is None:
+        out = torch.empty((B, N), dtype=torch.int32, device=x.device)
+    lib = nat.load()
+    ws_bytes = lib.fk_assign_workspace_size(B, K, nat.dtype_code(x.dtype))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    if status is None:
+        status = DeviceStatus.word(x.device)
+    with torch.cuda.device(x.device):
+        nat.check(lib.fk_assign_dot(
+            nat.ptr(x), nat.ptr(centroids), nat.ptr(out), nat.ptr(counts), nat.dtype_code(x.dtype),
+            B, N, K, D, nat.strides(x, 3), nat.strides(centroids, 3), nat.strides(out, 2),
+            nat.ptr(ws), ws_bytes, nat.ptr(status), nat.stream_handle(x.device)), "fk_assign_dot")
+    return out
+
+
+def finalize_normalized(sums, counts, old, new, shift_out=None, reset=False) -> None:
+    """Launch fk_centroid_finalize_normalized: new = normalize(counts ? sums / counts : old)."""
+    B, K, D = old.shape
+    lib = nat.load()
+    with torch.cuda.device(old.device):
+        nat.check(lib.fk_centroid_finalize_normalized(
+            nat.ptr(sums), nat.ptr(counts), nat.ptr(old), nat.ptr(new), nat.dtype_code(old.dtype),
+            B, K, D, nat.strides(old, 3), nat.strides(new, 3), nat.ptr(shift_out),
+            1 if reset else 0, nat.stream_handle(old.device)), "fk_centroid_finalize_normalized")

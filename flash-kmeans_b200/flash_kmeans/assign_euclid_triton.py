@@ -65,5 +65,20 @@ def euclid_assign_triton(
 
 def cosine_assign_triton(x: torch.Tensor, centroids: torch.Tensor, out: torch.Tensor = None,
                          *, BLOCK_N: int = 128, BLOCK_K: int = 128) -> torch.Tensor:
-    """Cosine assignment is outside the B200 build's scope (Euclidean Lloyd path only)."""
-    raise NotImplementedError("cosine assignment is not part of the B200 Euclidean build")
+    """Centroid of the largest dot product for every point; int32 (B, N).
+
+    Signature and contract of the reference wrapper (assign_euclid_triton.py:
+    1415-1498): x (B, N, D) and centroids (B, K, D) of one float dtype; with
+    normalised inputs this is the cosine assignment of batch_kmeans_Cosine,
+    otherwise the dot-product assignment of batch_kmeans_Dot.  Scores are
+    float32 dot products (3xTF32 for float32 inputs), ties go to the lowest
+    index.  The block sizes are accepted and ignored (one fixed tiling).
+    """
+    assert x.is_cuda and centroids.is_cuda, "All tensors must be on CUDA"
+    assert centroids.dtype == x.dtype, "centroids dtype mismatch"
+    B, N, D = x.shape
+    K = centroids.shape[1]
+    assert centroids.shape == (B, K, D), "centroids shape mismatch"
+    if out is None:
+        out = torch.empty((B, N), device=x.device, dtype=torch.int32)
+    return _ops.assign_dot(_ops.ensure_tma(x), _ops.ensure_tma(centroids), out=out)

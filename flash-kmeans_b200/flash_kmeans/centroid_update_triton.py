@@ -73,9 +73,36 @@ def triton_centroid_update_euclid(x: torch.Tensor, cluster_ids: torch.Tensor,
     return centroid_update_euclid(x, cluster_ids, old_centroids)
 
 
-def triton_centroid_update_cosine(x_norm, cluster_ids, old_centroids):
-    raise NotImplementedError("cosine update is not part of the B200 Euclidean build")
+def centroid_update_cosine(x_norm: torch.Tensor, cluster_ids: torch.Tensor,
+                           old_centroids: torch.Tensor) -> torch.Tensor:
+    """Per-cluster means, L2-normalised (the update of cosine / dot-product k-means).
+
+    Follows _centroid_update_torch_native with mode='cosine' (torch_fallback.py:
+    72-109): float32 sums and counts, mean (the old centroid, as float32, for an
+    empty cluster), F.normalize in float32, then cast to x's dtype.
+    """
+    assert x_norm.is_cuda and cluster_ids.is_cuda, "Inputs must be on CUDA device"
+    B, N, D = x_norm.shape
+    K = old_centroids.shape[1]
+    assert cluster_ids.shape == (B, N)
+    if cluster_ids.dtype not in (torch.int32, torch.int64):
+        raise TypeError("cluster_ids must be int32 or int64")
+    sums = torch.zeros((B, K, D), device=x_norm.device, dtype=torch.float32)
+    cnts = torch.zeros((B, K), device=x_norm.device, dtype=torch.int32)
+    _ops.accumulate(x_norm, cluster_ids, sums, cnts)
+    new = torch.empty((B, K, D), device=x_norm.device, dtype=x_norm.dtype)
+    _ops.finalize_normalized(sums, cnts, old_centroids.to(x_norm.dtype), new)
+    return new
 
 
-def triton_centroid_update_sorted_cosine(x_norm, cluster_ids, old_centroids, *, BLOCK_N: int = 256):
-    raise NotImplementedError("cosine update is not part of the B200 Euclidean build")
+def triton_centroid_update_cosine(x_norm: torch.Tensor, cluster_ids: torch.Tensor,
+                                  old_centroids: torch.Tensor) -> torch.Tensor:
+    """The reference's per-token variant (centroid_update_triton.py:73-119)."""
+    return centroid_update_cosine(x_norm, cluster_ids, old_centroids)
+
+
+def triton_centroid_update_sorted_cosine(x_norm: torch.Tensor, cluster_ids: torch.Tensor,
+                                         old_centroids: torch.Tensor, *,
+                                         BLOCK_N: int = 256) -> torch.Tensor:
+    """Signature of the reference (centroid_update_triton.py:268-313); BLOCK_N is ignored."""
+    return centroid_update_cosine(x_norm, cluster_ids, old_centroids)

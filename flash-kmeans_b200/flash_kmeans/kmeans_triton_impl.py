@@ -36,7 +36,14 @@ class LloydEngine:
     ``centroids`` the centroids that produced them.
     """
 
-    def __init__(self, B: int, N: int, K: int, D: int, dtype: torch.dtype, device):
+    def __init__(self, B: int, N: int, K: int, D: int, dtype: torch.dtype, device,
+                 metric: str = "euclid"):
+        """``metric``: "euclid" (nearest centroid, mean update) or "dot"
+        (largest dot product, L2-normalised mean update: the cosine and
+        dot-product k-means of the reference)."""
+        if metric not in ("euclid", "dot"):
+            raise ValueError(f"unknown metric {metric!r}")
+        self.metric = metric
         self.B, self.N, self.K, self.D, self.dtype = B, N, K, D, dtype
         self.device = torch.device(device)
         dev = self.device
@@ -51,9 +58,13 @@ class LloydEngine:
         self.stat_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
         self.csq_valid = False
         lib = nat.load()
-        self.ws = torch.empty(
-            lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype)),
-            dtype=torch.uint8, device=dev)
+        if metric == "euclid":
+            ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype))
+        else:  # fk_assign_dot, then fk_centroid_accumulate after it
+            self.ws_assign_bytes = lib.fk_assign_workspace_size(B, K, nat.dtype_code(dtype))
+            ws_bytes = -(-self.ws_assign_bytes // 256) * 256 + \
+                lib.fk_centroid_accumulate_workspace_size(B, N, K)
+        self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None
 
@@ -65,12 +76,15 @@ class LloydEngine:
         finalize; sorted -> c_sq staging, assignment, scan, scatter, segmented
         sum, finalize."""
         method = nat.load().fk_assign_accumulate_method(self.K, self.D, nat.dtype_code(self.dtype))
+        if self.metric == "dot":  # column mask, assignment, (privatised | sorted) sum, finalize
+            return 4 if method == nat.FK_ACC_PRIVATISED else 6
         return {nat.FK_ACC_PRIVATISED: 4, nat.FK_ACC_FUSED: 3}.get(method, 6)
 
     # ---------------------------------------------------------------- set-up
     def load(self, x: torch.Tensor, centroids: torch.Tensor, x_sq: torch.Tensor | None = None):
         self.x = _ops.ensure_tma(x)
-        self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
+        if self.metric == "euclid":
+            self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
         self.c_cur.copy_(centroids.view(self.B, self.K, self.D))
         self.csq_valid = False
         self.stat.zero_()
@@ -88,6 +102,9 @@ class LloydEngine:
         x, dev = self.x, self.device
         s = nat.stream_handle(dev)
         status = nat.ptr(self.stat[1:2])
+        if self.metric == "dot":
+            self._step_dot(lib, s, status, ev_assign)
+            return
         c_sq = self.csq if self.csq_valid else None
         if ev_assign is not None:
             ev_assign[0].record()
@@ -106,6 +123,32 @@ class LloydEngine:
             nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 1, s),
             "fk_centroid_finalize")
         self.csq_valid = True
+
+    def _step_dot(self, lib, s, status, ev_assign) -> None:
+        """Dot-product iteration: argmax assignment (labels and their counts),
+        per-cluster sums, L2-normalised means and the shift."""
+        B, N, K, D = self.B, self.N, self.K, self.D
+        x = self.x
+        wa = self.ws_assign_bytes
+        ws_acc = self.ws[-(-wa // 256) * 256:]
+        if ev_assign is not None:
+            ev_assign[0].record()
+        nat.check(lib.fk_assign_dot(
+            nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.ids), nat.ptr(self.hist),
+            nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
+            nat.strides(self.ids, 2), nat.ptr(self.ws), wa, status, s), "fk_assign_dot")
+        nat.check(lib.fk_centroid_accumulate(
+            nat.ptr(x), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.ptr(self.ids),
+            nat.FK_I32, nat.strides(self.ids, 2), nat.ptr(self.hist), nat.ptr(self.sums),
+            nat.ptr(self.hist), nat.ptr(ws_acc), ws_acc.numel(), status, s),
+            "fk_centroid_accumulate")
+        if ev_assign is not None:
+            ev_assign[1].record()
+        nat.check(lib.fk_centroid_finalize_normalized(
+            nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
+            nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
+            nat.strides(self.c_nxt, 3), nat.ptr(self.stat[0:1]), 1, s),
+            "fk_centroid_finalize_normalized")
 
     def advance(self) -> None:
         """Adopt the updated centroids for the next iteration."""
@@ -186,9 +229,64 @@ def batch_kmeans_Euclid(
         return eng.ids, eng.result_centroids(), it + 1
 
 
+def _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verbose, cosine):
+    name = "batch_kmeans_Cosine" if cosine else "batch_kmeans_Dot"
+    if not torch.cuda.is_available() or not x.is_cuda:
+        raise RuntimeError(f"{name} needs a CUDA tensor (this build has no CPU fallback)")
+    if max_iters < 1:
+        raise ValueError("max_iters must be >= 1")
+    B, N, D = x.shape
+    K = int(n_clusters)
+    with torch.cuda.device(x.device):
+        xs = _ops.row_normalize(x) if cosine else x
+        if init_centroids is None:
+            indices = torch.randint(0, N, (B, K), device=x.device)
+            centroids = torch.gather(xs, dim=1, index=indices[..., None].expand(-1, -1, D))
+        else:
+            centroids = init_centroids
+        centroids = centroids.view(B, K, D)
+        if cosine:
+            centroids = _ops.row_normalize(centroids)
+        eng = LloydEngine(B, N, K, D, x.dtype, x.device, metric="dot")
+        eng.load(xs, centroids)
+        need_sync = tol > 0 or verbose
+        tol_r = _round_tol(tol, x.dtype)
+        it = 0
+        for it in range(max_iters):
+            eng.step()
+            if need_sync:
+                shift, code = eng.read_stat()
+                eng.raise_on_status(code)
+                if verbose:
+                    tag = "" if cosine else " (dot)"
+                    print(f"Iter {it}{tag}, center shift: {shift:.6f}")
+                if shift < tol_r:
+                    break
+            eng.advance()
+        if not need_sync:
+            _, code = eng.read_stat()
+            eng.raise_on_status(code)
+        return eng.ids, eng.result_centroids(), it + 1
+
+
 def batch_kmeans_Cosine(x, n_clusters, max_iters=100, tol=0.0, init_centroids=None, verbose=False):
-    raise NotImplementedError("cosine k-means is not part of the B200 Euclidean build")
+    """Batched k-means by cosine similarity; reference kmeans_triton_impl.py:118-158.
+
+    x (B, N, D) is L2-normalised in its dtype, centroids start from normalised
+    random points (or ``init_centroids``, normalised), each iteration assigns
+    by the largest dot product and replaces each centroid by its cluster's
+    normalised mean.  On a tolerance break the centroids of the last
+    assignment are returned, as in the reference.
+    Returns cluster_ids (B, N) int32, centroids (B, K, D) x.dtype, iterations.
+    """
+    return _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verbose, True)
 
 
 def batch_kmeans_Dot(x, n_clusters, max_iters=100, tol=0.0, init_centroids=None, verbose=False):
-    raise NotImplementedError("dot-product k-means is not part of the B200 Euclidean build")
+    """Batched k-means by raw dot product; reference kmeans_triton_impl.py:161-188.
+
+    Like batch_kmeans_Cosine without normalising x or the initial centroids;
+    the update still normalises the cluster means (the reference's
+    _dot_iter uses the cosine update).
+    """
+    return _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verbose, False)

@@ -31,6 +31,16 @@
  *                             c_sq of assign_euclid_triton.py:1282-1283
  *   fk_pack_rows           <- no reference counterpart: repacks rows whose
  *                             stride is not a multiple of 16 bytes for TMA
+ *   fk_assign_dot          <- cosine_assign_triton, flash_kmeans/assign_euclid_triton.py:1415-1498
+ *                             (kernels _cosine_assign_kernel :1038-1131 and its split-D
+ *                             variant :1137-1231), used by batch_kmeans_Cosine / _Dot
+ *   fk_row_normalize       <- F.normalize of x in batch_kmeans_Cosine,
+ *                             flash_kmeans/kmeans_triton_impl.py:135
+ *   fk_centroid_finalize_normalized
+ *                          <- the cosine update's finalize: _centroid_update_torch_native
+ *                             with mode='cosine', flash_kmeans/torch_fallback.py:101-109
+ *                             (triton_centroid_update_sorted_cosine,
+ *                             centroid_update_triton.py:268-313)
  */
 #ifndef FLASH_KMEANS_B200_H
 #define FLASH_KMEANS_B200_H
@@ -82,6 +92,13 @@ int fk_row_sqnorm(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
                   const int64_t* x_strides3, void* out, int out_dtype,
                   const int64_t* out_strides2, void* stream);
 
+/* out = F.normalize(x, p=2, dim=-1) in x's dtype: norm accumulated in float32
+ * and rounded to the dtype, clamped below by 1e-12 taken in the dtype, each
+ * element divided in float32 and rounded.  out may alias x. */
+int fk_row_normalize(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
+                     const int64_t* x_strides3, void* out, const int64_t* out_strides3,
+                     void* stream);
+
 /* Copy x (B,N,D, any strides) into a contiguous (B,N,Dp) buffer, Dp >= D, with
  * zeros in columns [D, Dp).  Used to make rows TMA-addressable. */
 int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
@@ -104,6 +121,16 @@ int fk_assign(const void* x, const void* centroids, const void* x_sq, const void
               const int64_t* c_strides3, const int64_t* xsq_strides2,
               const int64_t* csq_strides2, const int64_t* out_strides2, void* workspace,
               size_t workspace_bytes, int32_t* dev_status, void* stream);
+
+/* Centroid of the largest dot product (cosine / dot-product k-means):
+ * out[b,n] = argmax_k x[b,n].c[b,k] with float32 (16-bit inputs) or 3xTF32
+ * (float32 inputs) dot products, lowest index on ties.  Same conventions and
+ * workspace (fk_assign_workspace_size) as fk_assign, without x_sq / c_sq;
+ * counts optional as there. */
+int fk_assign_dot(const void* x, const void* centroids, int32_t* out, int32_t* counts, int dtype,
+                  int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
+                  const int64_t* c_strides3, const int64_t* out_strides2, void* workspace,
+                  size_t workspace_bytes, int32_t* dev_status, void* stream);
 
 /* Assignment fused with the centroid accumulation of one Lloyd iteration
  * (replaces the pair euclid_assign_triton + triton_centroid_update_sorted_euclid
@@ -176,6 +203,15 @@ int fk_centroid_finalize(float* sums, int32_t* counts, const void* old_centroids
                          void* new_centroids, int dtype, int64_t B, int64_t K, int64_t D,
                          const int64_t* old_strides3, const int64_t* new_strides3,
                          float* csq_out, float* shift_out, int reset_accumulators, void* stream);
+
+/* Cosine / dot-product finalize: m = counts ? sums / counts : old (float32),
+ * new = (m / max(||m||, 1e-12)) cast to dtype; shift_out as in
+ * fk_centroid_finalize; reset_accumulators as there. */
+int fk_centroid_finalize_normalized(float* sums, int32_t* counts, const void* old_centroids,
+                                    void* new_centroids, int dtype, int64_t B, int64_t K,
+                                    int64_t D, const int64_t* old_strides3,
+                                    const int64_t* new_strides3, float* shift_out,
+                                    int reset_accumulators, void* stream);
 
 #ifdef __cplusplus
 }

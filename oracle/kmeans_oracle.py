@@ -253,6 +253,91 @@ def kmeans_large_n(x, n_clusters: int, max_iters: int = 100, tol: float = 0.0,
 
 
 # --------------------------------------------------------------------------
+# cosine / dot-product k-means
+# --------------------------------------------------------------------------
+def normalize_rows(x, dtype: str) -> np.ndarray:
+    """``F.normalize(x, p=2, dim=-1)`` in ``dtype`` (kmeans_triton_impl.py:135,148).
+
+    The norm accumulates in float32 (here float64, then rounded to float32) and
+    rounds to the dtype; it is clamped below by eps = 1e-12 taken in the dtype
+    (0 for float16); every element is divided in float32 and rounded.
+    """
+    x = np.asarray(x, np.float32)
+    ss = (x.astype(np.float64) ** 2).sum(-1, keepdims=True)
+    norm = round_to(np.sqrt(ss).astype(np.float32), dtype)
+    eps = round_to(np.float32(1e-12), dtype)
+    den = np.maximum(norm, eps)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        return round_to(x / den, dtype)
+
+
+def scores_f64(x, centroids) -> np.ndarray:
+    """Exact (float64) dot products x . c^T per batch."""
+    x = np.asarray(x, np.float64)
+    c = np.asarray(centroids, np.float64)
+    return np.einsum("bnd,bkd->bnk", x, c)
+
+
+def assign_dot(x, centroids) -> np.ndarray:
+    """Largest dot product, lowest index on ties: the reference's own check of
+    ``cosine_assign_triton`` (examples/test_assign_dtype_d.py:101-106, argmax
+    of a float32 einsum), and the einsum/argmax stated in _cosine_iter
+    (kmeans_triton_impl.py:20-23).  Scores are exact here; the float32 scores
+    of a kernel differ only on near-ties, which the parity bar excuses."""
+    return scores_f64(x, centroids).argmax(-1).astype(np.int32)
+
+
+def finalize_normalized(sums, cnts, old_centroids, dtype: str):
+    """Mean, keep-old-if-empty, F.normalize in float32, cast: the mode='cosine'
+    finalize of ``_centroid_update_torch_native`` (torch_fallback.py:101-109)."""
+    cnt = np.asarray(cnts, dtype=np.float32)[..., None]
+    empty = cnt == 0
+    mean = np.asarray(sums, dtype=np.float32) / np.maximum(cnt, 1.0)
+    new = np.where(empty, np.asarray(old_centroids, dtype=np.float32), mean).astype(np.float32)
+    norm = np.sqrt((new.astype(np.float64) ** 2).sum(-1, keepdims=True)).astype(np.float32)
+    return round_to(new / np.maximum(norm, np.float32(1e-12)), dtype)
+
+
+def centroid_update_cosine(x, ids, old_centroids, dtype: str, exact_order: bool = True):
+    """``_centroid_update_torch_native(..., mode='cosine')`` (torch_fallback.py:72-109)."""
+    K = np.asarray(old_centroids).shape[1]
+    sums, cnts = centroid_sums(x, ids, K, exact_order=exact_order)
+    return finalize_normalized(sums, cnts, old_centroids, dtype)
+
+
+def batch_kmeans_similarity(x, n_clusters: int, max_iters: int = 100, tol: float = 0.0,
+                            init_centroids=None, dtype: str = "float32", cosine: bool = True,
+                            exact_order: bool = True, history: list | None = None):
+    """``batch_kmeans_Cosine`` (cosine=True, kmeans_triton_impl.py:118-158) and
+    ``batch_kmeans_Dot`` (cosine=False, :161-188): x (and the initial
+    centroids) normalised for cosine; each iteration assigns by the largest dot
+    product and takes the normalised cluster means (both use the cosine
+    update); the tolerance break returns the centroids of the last assignment.
+    ``init_centroids`` (B, K, D) is required; ``history`` as in
+    ``batch_kmeans_euclid``."""
+    x = round_to(x, dtype)
+    B, N, D = x.shape
+    if init_centroids is None:
+        raise ValueError("the oracle needs explicit init_centroids")
+    xs = normalize_rows(x, dtype) if cosine else x
+    c = round_to(np.asarray(init_centroids, np.float32).reshape(B, n_clusters, D), dtype)
+    if cosine:
+        c = normalize_rows(c, dtype)
+    ids = None
+    it = 0
+    for it in range(max_iters):
+        ids = assign_dot(xs, c)
+        new = centroid_update_cosine(xs, ids, c, dtype, exact_order=exact_order)
+        shift = center_shift(new, c, dtype)
+        if history is not None:
+            history.append((c, ids, new, shift))
+        if shift_below_tol(shift, tol, dtype):
+            break
+        c = new
+    return ids, c, it + 1
+
+
+# --------------------------------------------------------------------------
 # synthetic inputs (seeded; numpy PCG64 streams are stable across versions)
 # --------------------------------------------------------------------------
 def gmm_points(rng: np.random.Generator, B: int, N: int, D: int, n_comp: int,

@@ -8,6 +8,9 @@ The bar (from the project's north star):
   least one is allowed, so a case under 1000 points is not failed by a single
   near-tie that the tensor core's summation order legitimately breaks the
   other way);
+* for the dot-product (cosine / dot k-means) labels the gap is the exact score
+  difference ``|x.c_a - x.c_b|`` relative to ``||x|| max(||c_a||, ||c_b||)``,
+  with the same tolerances;
 * centroids agree within 1e-3 relative per centroid:
   ``||dc_k|| <= 1e-3 * max(||c_k||, 1e-3 * max_j ||c_j||)``.
 """
@@ -22,8 +25,9 @@ MAX_EXCUSED_FRAC = 1e-3
 CENTROID_RTOL = 1e-3
 
 
-def label_report(x, centroids, got, want, dtype):
-    """Compare two labelings of x against centroids; returns a dict."""
+def label_report(x, centroids, got, want, dtype, metric="euclid"):
+    """Compare two labelings of x against centroids; returns a dict.
+    ``metric`` is "euclid" (nearest centroid) or "dot" (largest dot product)."""
     got = np.asarray(got).astype(np.int64).reshape(np.asarray(want).shape)
     want = np.asarray(want).astype(np.int64)
     mism = got != want
@@ -37,9 +41,16 @@ def label_report(x, centroids, got, want, dtype):
     xs = x[bi, ni]
     ca = c[bi, got[bi, ni]]
     cb = c[bi, want[bi, ni]]
-    da = ((xs - ca) ** 2).sum(-1)
-    db = ((xs - cb) ** 2).sum(-1)
-    gap = np.abs(da - db) / (np.minimum(np.abs(da), np.abs(db)) + 1e-3)
+    if metric == "dot":
+        sa = (xs * ca).sum(-1)
+        sb = (xs * cb).sum(-1)
+        scale = np.linalg.norm(xs, axis=-1) * np.maximum(np.linalg.norm(ca, axis=-1),
+                                                         np.linalg.norm(cb, axis=-1))
+        gap = np.abs(sa - sb) / (scale + 1e-30)
+    else:
+        da = ((xs - ca) ** 2).sum(-1)
+        db = ((xs - cb) ** 2).sum(-1)
+        gap = np.abs(da - db) / (np.minimum(np.abs(da), np.abs(db)) + 1e-3)
     tol = LABEL_TOL[dtype]
     out["excused"] = int((gap < tol).sum())
     out["bad"] = int((gap >= tol).sum())
@@ -47,8 +58,8 @@ def label_report(x, centroids, got, want, dtype):
     return out
 
 
-def assert_labels(x, centroids, got, want, dtype, what=""):
-    r = label_report(x, centroids, got, want, dtype)
+def assert_labels(x, centroids, got, want, dtype, what="", metric="euclid"):
+    r = label_report(x, centroids, got, want, dtype, metric)
     assert r["bad"] == 0, f"{what}: {r['bad']} label mismatches beyond near-tie tolerance {r}"
     allowed = max(1, int(np.ceil(MAX_EXCUSED_FRAC * r["n"])))
     assert r["excused"] <= allowed, f"{what}: too many near-tie mismatches {r}"

@@ -103,3 +103,70 @@ def checksum(*arrays) -> float:
 
 def path(name: str) -> str:
     return os.path.join(GOLDEN_DIR, name + ".npz")
+
+
+# cosine / dot-product k-means (the reference's batch_kmeans_Cosine / _Dot path)
+NORMALIZE_CASES = [
+    dict(name="normalize_f16", dtype="float16", B=2, N=333, D=100, seed=41),
+    dict(name="normalize_bf16", dtype="bfloat16", B=1, N=500, D=64, seed=42),
+    dict(name="normalize_f32", dtype="float32", B=2, N=257, D=33, seed=43),
+]
+
+SIM_ASSIGN_CASES = [
+    dict(name="cos_assign_f16", dtype="float16", B=2, N=1000, K=70, D=128, seed=51, cosine=True),
+    dict(name="cos_assign_bf16", dtype="bfloat16", B=1, N=1500, K=300, D=64, seed=52, cosine=True),
+    dict(name="cos_assign_f32", dtype="float32", B=2, N=700, K=45, D=96, seed=53, cosine=True),
+    dict(name="dot_assign_f16_d17", dtype="float16", B=1, N=513, K=33, D=17, seed=54, cosine=False,
+         neg=True),
+    dict(name="dot_assign_f32_k1031", dtype="float32", B=1, N=2049, K=1031, D=128, seed=55,
+         cosine=False),
+]
+
+SIM_UPDATE_CASES = [
+    dict(name="cos_update_f16", dtype="float16", B=2, N=900, K=40, D=64, seed=61, holes=4),
+    dict(name="cos_update_bf16", dtype="bfloat16", B=1, N=1200, K=100, D=128, seed=62, holes=6),
+    dict(name="cos_update_f32", dtype="float32", B=2, N=500, K=23, D=48, seed=63, holes=3),
+]
+
+SIM_LLOYD_CASES = [
+    dict(name="cos_lloyd_f16", dtype="float16", B=2, N=3000, K=40, D=64, seed=71,
+         comps=40, mean_std=2.0, iters=4, cosine=True),
+    dict(name="cos_lloyd_f32", dtype="float32", B=1, N=2048, K=32, D=128, seed=72,
+         comps=32, mean_std=2.0, iters=4, cosine=True),
+    dict(name="dot_lloyd_f16", dtype="float16", B=1, N=2000, K=16, D=32, seed=73,
+         comps=16, mean_std=2.0, iters=3, cosine=False),
+]
+
+
+def normalize_inputs(spec):
+    """Gaussian rows in the dtype, row 5 of batch 0 all zeros (the eps clamp)."""
+    rng = np.random.default_rng(spec["seed"])
+    x = ko.round_to(rng.standard_normal((spec["B"], spec["N"], spec["D"]), dtype=np.float32)
+                    * 3.0, spec["dtype"])
+    x[0, 5] = 0.0
+    return x
+
+
+def sim_assign_inputs(spec):
+    """Points and centroids in the dtype (normalised by F.normalize afterwards
+    when ``cosine``).  ``neg``: non-negative points and non-positive
+    centroids, so every score, the winning one included, is negative."""
+    rng = np.random.default_rng(spec["seed"])
+    B, N, K, D, dt = spec["B"], spec["N"], spec["K"], spec["D"], spec["dtype"]
+    x = rng.standard_normal((B, N, D), dtype=np.float32)
+    c = rng.standard_normal((B, K, D), dtype=np.float32)
+    if spec.get("neg"):
+        x, c = np.abs(x), -np.abs(c)
+    return ko.round_to(x, dt), ko.round_to(c, dt)
+
+
+def sim_update_inputs(spec):
+    return update_inputs(spec)
+
+
+def sim_lloyd_inputs(spec):
+    rng = np.random.default_rng(spec["seed"])
+    B, N, K, D, dt = spec["B"], spec["N"], spec["K"], spec["D"], spec["dtype"]
+    x = ko.round_to(ko.gmm_points(rng, B, N, D, spec["comps"], spec["mean_std"]), dt)
+    c0 = ko.init_from_points(rng, x, K, replace=False)
+    return x, c0

@@ -13,7 +13,17 @@ the project's parity oracle) and records, for every spec in ``cases.py``:
 * update: ``_centroid_update_torch_native`` centroids (torch_fallback.py:72-108);
 * Lloyd: per-iteration ``_euclid_iter_torch_naive`` outputs
   (torch_fallback.py:111-135) and the final ``batch_kmeans_Euclid_torch_native``
-  result (torch_fallback.py:137-178).
+  result (torch_fallback.py:137-178);
+* cosine / dot: ``F.normalize`` rows (kmeans_triton_impl.py:135), the argmax of
+  the float32 einsum the reference checks ``cosine_assign_triton`` against
+  (examples/test_assign_dtype_d.py:101-106), ``_centroid_update_torch_native``
+  with ``mode='cosine'`` (torch_fallback.py:72-109), and Lloyd chains made of
+  those steps in the order of ``_cosine_iter`` / ``_dot_iter``
+  (kmeans_triton_impl.py:19-35) driven as ``batch_kmeans_Cosine`` / ``_Dot``
+  drive them (kmeans_triton_impl.py:118-188).
+
+An optional second argument names the groups to (re)write, comma separated:
+``assign,update,lloyd,normalize,sim`` (default: all).
 
 Inputs are rebuilt from their seeds by ``cases.py``; fixtures store outputs and
 an input checksum.  Nothing at test time reads the reference checkout.
@@ -41,12 +51,27 @@ def _np(t):
     return t.detach().to(torch.float32).numpy()
 
 
-def main(ref_root: str) -> None:
+GROUPS = ("assign", "update", "lloyd", "normalize", "sim")
+
+
+def main(ref_root: str, groups=GROUPS) -> None:
     sys.path.insert(0, ref_root)
     from flash_kmeans import torch_fallback as tf  # the reference's oracle
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if "assign" in groups:
+        _assign(tf)
+    if "update" in groups:
+        _update(tf)
+    if "lloyd" in groups:
+        _lloyd(tf)
+    if "normalize" in groups:
+        _normalize()
+    if "sim" in groups:
+        _similarity(tf)
 
+
+def _assign(tf):
     for spec in cases.ASSIGN_CASES:
         x, c, xsq, xsq_dtype = cases.assign_inputs(spec)
         dt = spec["dtype"]
@@ -55,6 +80,8 @@ def main(ref_root: str) -> None:
                             checksum=cases.checksum(x, c, xsq))
         print("wrote", spec["name"])
 
+
+def _update(tf):
     for spec in cases.UPDATE_CASES:
         x, ids, old = cases.update_inputs(spec)
         dt = spec["dtype"]
@@ -63,6 +90,8 @@ def main(ref_root: str) -> None:
                             checksum=cases.checksum(x, ids, old))
         print("wrote", spec["name"])
 
+
+def _lloyd(tf):
     for spec in cases.LLOYD_CASES:
         x, c0 = cases.lloyd_inputs(spec)
         dt = spec["dtype"]
@@ -92,7 +121,67 @@ def main(ref_root: str) -> None:
         print("wrote", spec["name"], "n_iters", n_it)
 
 
+def _normalize():
+    import torch.nn.functional as F
+    for spec in cases.NORMALIZE_CASES:
+        x = cases.normalize_inputs(spec)
+        y = F.normalize(_t(x, spec["dtype"]), p=2, dim=-1)
+        np.savez_compressed(cases.path(spec["name"]), y=_np(y), checksum=cases.checksum(x))
+        print("wrote", spec["name"])
+
+
+def _scores_argmax(xs, c):
+    # the float32 einsum + argmax of examples/test_assign_dtype_d.py:101-106
+    return torch.einsum("bnd,bkd->bnk", xs.float(), c.float()).argmax(dim=-1)
+
+
+def _similarity(tf):
+    import torch.nn.functional as F
+    for spec in cases.SIM_ASSIGN_CASES:
+        x, c = cases.sim_assign_inputs(spec)
+        xt, ct = _t(x, spec["dtype"]), _t(c, spec["dtype"])
+        if spec["cosine"]:
+            xt, ct = F.normalize(xt, dim=-1), F.normalize(ct, dim=-1)
+        ids = _scores_argmax(xt, ct)
+        np.savez_compressed(cases.path(spec["name"]), ids=ids.numpy().astype(np.int32),
+                            checksum=cases.checksum(x, c))
+        print("wrote", spec["name"])
+
+    for spec in cases.SIM_UPDATE_CASES:
+        x, ids, old = cases.sim_update_inputs(spec)
+        dt = spec["dtype"]
+        xs = F.normalize(_t(x, dt), dim=-1)
+        new = tf._centroid_update_torch_native(xs, torch.from_numpy(ids).long(), _t(old, dt),
+                                               mode="cosine")
+        np.savez_compressed(cases.path(spec["name"]), centroids=_np(new),
+                            checksum=cases.checksum(x, ids, old))
+        print("wrote", spec["name"])
+
+    for spec in cases.SIM_LLOYD_CASES:
+        x, c0 = cases.sim_lloyd_inputs(spec)
+        dt, cosine = spec["dtype"], spec["cosine"]
+        B, K, D = spec["B"], spec["K"], spec["D"]
+        xs = _t(x, dt)
+        cent = _t(c0, dt).view(B, K, D)
+        if cosine:
+            xs, cent = F.normalize(xs, p=2, dim=-1), F.normalize(cent, p=2, dim=-1)
+        init = cent.clone()
+        ids_hist, cent_hist, shifts = [], [], []
+        for _ in range(spec["iters"]):
+            ids = _scores_argmax(xs, cent)
+            new = tf._centroid_update_torch_native(xs, ids, cent, mode="cosine")
+            shifts.append(float((new - cent).norm(dim=-1).max()))
+            ids_hist.append(ids.numpy().astype(np.int16))
+            cent_hist.append(_np(new))
+            cent = new.clone()
+        np.savez_compressed(cases.path(spec["name"]), init=_np(init),
+                            trace_ids=np.stack(ids_hist), trace_centroids=np.stack(cent_hist),
+                            trace_shifts=np.asarray(shifts, np.float32),
+                            checksum=cases.checksum(x, c0))
+        print("wrote", spec["name"], "shifts", shifts)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py /path/to/flash-kmeans-checkout")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden.py /path/to/flash-kmeans-checkout [group,...]")
+    main(sys.argv[1], tuple(sys.argv[2].split(",")) if len(sys.argv) == 3 else GROUPS)

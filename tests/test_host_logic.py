@@ -71,11 +71,10 @@ def test_flashkmeans_validation_errors():
     assert km.fit is not None and km.fit_predict is not None
 
 
-def test_cosine_and_dot_raise_not_implemented():
-    with pytest.raises(NotImplementedError):
-        flash_kmeans.batch_kmeans_Cosine(torch.randn(1, 4, 4), 2)
-    with pytest.raises(NotImplementedError):
-        flash_kmeans.batch_kmeans_Dot(torch.randn(1, 4, 4), 2)
+def test_cosine_and_dot_have_no_cpu_fallback():
+    for fn in (flash_kmeans.batch_kmeans_Cosine, flash_kmeans.batch_kmeans_Dot):
+        with pytest.raises(RuntimeError, match="no CPU fallback"):
+            fn(torch.randn(1, 4, 4), 2)
 
 
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32])
