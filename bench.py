@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload cfg2|cfg1|cfg3|cfg4|cfg5] [--op lloyd|assign] [--stream]
+                    [--metric euclid|cosine|dot]
 
 A step is one Lloyd iteration (assign + update + shift check) over the whole
 batch of the workload.  Default workload: BASELINE config 2 (B=32, N=75600,
@@ -25,6 +26,9 @@ D=128, K=8192, fp32) with x in pinned host memory, N partitioned over the
 ranks (strong scaling, NCCL all-reduce of the partial sums); each rank's shard
 stays resident in HBM after the first pass when it fits, `--stream` re-streams
 it every iteration instead.
+`--metric cosine|dot`: the same step for batch_kmeans_Cosine / batch_kmeans_Dot
+(dot-product argmax assignment, normalised-mean update; x row-normalised
+once, outside the timed region, for cosine); the CPU leg is skipped.
 """
 from __future__ import annotations
 
@@ -218,21 +222,28 @@ def _peaks():
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
-    from flash_kmeans import batch_kmeans_Euclid
+    import flash_kmeans
+    from flash_kmeans import _ops
     from flash_kmeans.kmeans_triton_impl import LloydEngine
 
     w = WORKLOADS[args.workload]
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     B, N, D, K = w["B"], w["N"], w["D"], w["K"]
+    sim = args.metric != "euclid"
+    driver = {"euclid": flash_kmeans.batch_kmeans_Euclid, "cosine": flash_kmeans.batch_kmeans_Cosine,
+              "dot": flash_kmeans.batch_kmeans_Dot}[args.metric]
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not sim:
         cpu = CpuOracle(w)  # spawn before heavy GPU work
 
     x, c0 = _make_inputs(w, dev, seed=1234 + rank)
-    eng = LloydEngine(B, N, K, D, x.dtype, dev)
-    eng.load(x, c0)
+    eng = LloydEngine(B, N, K, D, x.dtype, dev, metric="dot" if sim else "euclid")
+    if args.metric == "cosine":
+        eng.load(_ops.row_normalize(x), _ops.row_normalize(c0))
+    else:
+        eng.load(x, c0)
     torch.cuda.synchronize()
 
     steps, warm = args.steps, args.warmup
@@ -288,7 +299,7 @@ def run_ours(args, rank, world, local_rank):
             f0.record()
             xd = x_h.to(dev, non_blocking=True)
             cd = c_h.to(dev, non_blocking=True)
-            ids, cent, n_it = batch_kmeans_Euclid(xd, K, max_iters=20, tol=1e-4, init_centroids=cd)
+            ids, cent, n_it = driver(xd, K, max_iters=20, tol=1e-4, init_centroids=cd)
             ids_h = ids.to("cpu")
             cent_h = cent.to("cpu")
             f1.record()
@@ -306,7 +317,7 @@ def run_ours(args, rank, world, local_rank):
                "h2d_bytes_per_step": int(x_h.numel() * x_h.element_size()
                                          + c_h.numel() * c_h.element_size()),
                "d2h_bytes_per_step": int(ids_h.numel() * 4 + cent_h.numel() * cent_h.element_size()),
-               "step": "batch_kmeans_Euclid(max_iters=20, tol=1e-4) on x copied from pinned host, "
+               "step": f"{driver.__name__}(max_iters=20, tol=1e-4) on x copied from pinned host, "
                        "labels+centroids copied back",
                "iters_per_step": iters_total / args.e2e_steps}
 
@@ -326,6 +337,7 @@ def run_ours(args, rank, world, local_rank):
             "dtype": "f16" if w["dtype"] == "float16" else ("bf16" if w["dtype"] == "bfloat16" else "f32(3xTF32)"),
             "data": "synthetic (seeded torch generator; shapes/distribution of the BASELINE config)",
             "config": {"workload": _describe(args.workload, w),
+                       "metric": args.metric,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs exceed the 126 MB L2 (x is %d MB); no flush" %
                              (B * N * D * (2 if w["dtype"] != "float32" else 4) // 2 ** 20),
@@ -336,7 +348,7 @@ def run_ours(args, rank, world, local_rank):
                          "unit": UNIT, "frac": round(achieved / burst, 4),
                          "peak_source": f"{src} dense bf16 (burst)",
                          "frac_of_sustained": round(achieved / sustained, 4) if sustained else None,
-                         "traffic": _load_traffic(args.workload)},
+                         "traffic": None if sim else _load_traffic(args.workload)},
             "e2e": e2e,
             "cpu_baseline": cpu_baseline,
             "gpu_launches": eng.kernels_per_step * steps,
@@ -565,6 +577,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=["lloyd", "assign"], default="lloyd")
+    ap.add_argument("--metric", choices=["euclid", "cosine", "dot"], default="euclid")
     ap.add_argument("--stream", action="store_true",
                     help="cfg5: stream x from host every iteration even when it fits in HBM")
     args = ap.parse_args()

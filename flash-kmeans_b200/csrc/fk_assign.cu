@@ -31,9 +31,9 @@
 //      float32 chain.
 //   3  16-bit x, dot-product argmax (cosine / dot k-means, replaces
 //      _cosine_assign_kernel, assign_euclid_triton.py:1038-1131): the float32
-//      cross itself, maximised; run as the argmin of -cross + m, m = 0 for real
-//      centroids and +inf for padding columns (the c_sq slot), so padding never
-//      wins even when every real score is negative.
+//      cross itself, maximised (ArgmaxSaved); padding columns are set to -inf
+//      in the chunk that crosses K, so they never win even when every real
+//      score is negative.  No c_sq.
 //   4  float32 x, dot-product argmax with the 3xTF32 cross of mode 2.
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
@@ -83,11 +83,12 @@ struct Layout {
   static constexpr int merge_bytes = 2 * (kGroups - 1) * kRows * 8;
   static constexpr int lab_off = merge_off + merge_bytes;
   static constexpr int lab_bytes = FUSE ? 2 * kRows * 4 : 0;  // [parity][row] label or -1
-  // mode 0: each epilogue thread's saved chunk of 16 packed distances, as
-  // [unit 0..3][epilogue thread] 16-byte units (conflict-free stores)
+  // modes 0, 3, 4: each epilogue thread's saved chunk (16 packed distances,
+  // or 16 float32 scores), as [unit 0..3][epilogue thread] 16-byte units
+  // (conflict-free stores)
   static constexpr int save_stride = EPI * 32;  // in 16-byte units
   static constexpr int save_off = lab_off + lab_bytes;
-  static constexpr int save_bytes = (MODE == 0) ? 4 * save_stride * 16 : 0;
+  static constexpr int save_bytes = (MODE == 0 || MODE >= 3) ? 4 * save_stride * 16 : 0;
   static constexpr int bar_off = save_off + save_bytes;
   // x_full[XB] x_empty[XB] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
@@ -298,8 +299,7 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
       const int c = j % kChains;
       float cr = __uint_as_float(v[j]);
       if constexpr (MODE == 1) cr = round16<T>(cr);
-      // modes 3/4: argmax of the score as argmin of -score (+inf on padding)
-      const float d = MODE >= 3 ? __fadd_rn(-cr, cs[j]) : __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
+      const float d = __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
       const bool lt = d < best[c];
       best[c] = fminf(best[c], d);
       loc[c] = lt ? j : loc[c];
@@ -318,6 +318,69 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
         idx = i;
       }
     }
+  }
+};
+
+// Modes 3 and 4 (dot-product argmax): float32 scores straight from TMEM.  Per
+// 16-column half of a chunk a tree of fmaxf gives the half's maximum; only a
+// strictly larger maximum replaces the running best (so the earliest half
+// keeps a tie) and then the half's 16 scores go to this thread's shared-memory
+// slot.  result() scans the saved half for the first score equal to the best.
+// Padding columns (>= K, zero-filled centroid rows) only occur in the chunk
+// that crosses K: that chunk sets them to -inf first (a warp-uniform branch).
+// A point whose scores are all NaN keeps nothing and reports its first
+// column with +inf, so the merge gives column 0, as argmax over NaNs does.
+struct ArgmaxSaved {
+  float best;   // running maximum
+  int part;     // col >> 4 of the saved half chunk, -1 while nothing is saved
+  uint4* slot;  // this thread's four 16-byte units, `stride` units apart
+  int stride;
+  __device__ __forceinline__ void init(uint4* s, int st) {
+    best = __int_as_float(0xff800000);
+    part = -1;
+    slot = s;
+    stride = st;
+  }
+  __device__ __forceinline__ void half16(const uint32_t* v, int part16) {
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
+    const float mm = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
+    if (mm > best) {
+      best = mm;
+      part = part16;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        slot[u * stride] = make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    }
+  }
+  __device__ __forceinline__ void chunk32(uint32_t (&v)[32], int col0, int K) {
+    if (col0 + 32 > K) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = (col0 + j < K) ? v[j] : 0xff800000u;
+    }
+    half16(v, col0 >> 4);
+    half16(v + 16, (col0 >> 4) + 1);
+  }
+  // val is the negated score, so the group merge (smallest value, then lowest
+  // column) is the argmax with first-index ties
+  __device__ __forceinline__ void result(float& val, int& idx, int first_col) const {
+    val = __int_as_float(0x7f800000);
+    idx = first_col;
+    if (part < 0) return;
+    val = -best;
+    int pos = 15;
+#pragma unroll
+    for (int u = 3; u >= 0; --u) {
+      const uint4 q = slot[u * stride];
+      if (__uint_as_float(q.w) == best) pos = 4 * u + 3;
+      if (__uint_as_float(q.z) == best) pos = 4 * u + 2;
+      if (__uint_as_float(q.y) == best) pos = 4 * u + 1;
+      if (__uint_as_float(q.x) == best) pos = 4 * u;
+    }
+    idx = part * 16 + pos;
   }
 };
 
@@ -601,9 +664,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       const float xsq_f = xsq_next;
       if (t + 1 < t_end) xsq_next = load_xsq(t + 1);
 
-      using Argmin = typename std::conditional<MODE == 0, ArgminSaved<T>, ArgminF32<T, MODE>>::type;
+      using Argmin = typename std::conditional<
+          MODE == 0, ArgminSaved<T>,
+          typename std::conditional<(MODE >= 3), ArgmaxSaved, ArgminF32<T, MODE>>::type>::type;
       Argmin am;
-      if constexpr (MODE == 0)
+      if constexpr (MODE == 0 || MODE >= 3)
         am.init(reinterpret_cast<uint4*>(smem + L::save_off) + ew * 32 + lane, L::save_stride);
       else
         am.init();
@@ -655,10 +720,12 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           if (++ab == kAcc) { ab = 0; aph ^= 1; }
         }
       };
-      auto reduce = [&](int g, const uint32_t(&v)[32], const uint4(&cq)[kCsqVec]) {
+      auto reduce = [&](int g, uint32_t(&v)[32], const uint4(&cq)[kCsqVec]) {
         const int col0 = (g / kGChunks) * kCent + h * kGCols + (g % kGChunks) * 32;
         if constexpr (MODE == 0) {
           am.chunk32(v, reinterpret_cast<const uint32_t*>(cq), xsq2, col0);
+        } else if constexpr (MODE >= 3) {
+          am.chunk32(v, col0, p.K);
         } else {
           const float4* src = reinterpret_cast<const float4*>(csq_row + col0 * 4);
           float4 c4[8];
@@ -693,7 +760,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       // Per-thread winner: (value, lowest column on ties).
       float val;
       int idx;
-      if constexpr (MODE == 0)
+      if constexpr (MODE == 0 || MODE >= 3)
         am.result(val, idx, h * kGCols);
       else
         am.result(val, idx);
@@ -926,13 +993,6 @@ __global__ void copy_csq_kernel(const void* __restrict__ csq_in, int csq_dtype, 
   }
 }
 
-// Dot-product modes: 0 for real centroids, +inf for the padding columns.
-__global__ void dot_mask_kernel(float* __restrict__ out, int64_t kpad, int K, int64_t total) {
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < total;
-       r += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    out[r] = static_cast<int>(r % kpad) < K ? 0.0f : __int_as_float(0x7f800000);
-}
-
 template <typename T>
 static int assign_typed(const void* x, const void* cent, const void* x_sq, const void* c_sq,
                         int32_t* out, int32_t* counts, int xsq_dtype, int csq_dtype, int64_t B,
@@ -948,18 +1008,15 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   const bool xres = is16 && nd <= kResidentChunks;
   // K <= 128 (one centroid tile either way): 128-column tiles, so the epilogue
   // skips the padding half of a 256-column tile and TMEM holds four accumulators
-  const bool narrow = is16 && !sums && !dot && K <= kCent / 2;
+  const bool narrow = is16 && !sums && K <= kCent / 2;
   const int kc = narrow ? kCent / 2 : kCent;
   const int nkt = static_cast<int>((K + kc - 1) / kc);
   const int64_t kpad = static_cast<int64_t>(nkt) * kc;
 
-  // 1) padded c_sq in the distance dtype (the 0 / +inf column mask for dot modes)
+  // 1) padded c_sq in the distance dtype (the dot-product modes have none:
+  //    their epilogue masks the padding columns itself)
   if (dot) {
-    const int64_t total = B * kpad;
-    const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-    dot_mask_kernel<<<blocks, 256, 0, stream>>>(static_cast<float*>(ws), kpad, (int)K, total);
-    int st = check_launch("dot_mask_kernel");
-    if (st != FK_OK) return st;
+    // nothing to stage
   } else if (c_sq) {
     const int64_t total = B * kpad;
     const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
@@ -1023,12 +1080,20 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.status = status;
 
   if (dot) {
-    if (sums) return fail(FK_ERR_UNSUPPORTED, "fused sums are not built for dot-product modes");
-    if constexpr (Elem<T>::kBytes == 2)
+    if constexpr (Elem<T>::kBytes == 2) {
+      if (sums) {
+        if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
+        return launch_assign<T, 3, true, true>(tx, tc, p, stream);
+      }
+      if (narrow)
+        return xres ? launch_assign<T, 3, true, false, kCent / 2, true>(tx, tc, p, stream)
+                    : launch_assign<T, 3, false, false, kCent / 2>(tx, tc, p, stream);
       return xres ? launch_assign<T, 3, true>(tx, tc, p, stream)
                   : launch_assign<T, 3, false>(tx, tc, p, stream);
-    else
+    } else {
+      if (sums) return fail(FK_ERR_UNSUPPORTED, "fused sums need 16-bit x");
       return launch_assign<T, 4, false>(tx, tc, p, stream);
+    }
   }
   if constexpr (Elem<T>::kBytes == 2) {
     if (sums) {  // fused centroid sums: resident x tiles only (checked by the caller)
@@ -1181,26 +1246,31 @@ extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int6
          fk_centroid_accumulate_workspace_size(B, N, K);
 }
 
-extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq,
-                                    const void* c_sq, int32_t* out, int32_t* counts, float* sums,
-                                    int dtype, int xsq_dtype, int csq_dtype, int64_t B, int64_t N,
-                                    int64_t K, int64_t D, const int64_t* x_strides3,
-                                    const int64_t* c_strides3, const int64_t* xsq_strides2,
-                                    const int64_t* csq_strides2, const int64_t* out_strides2,
-                                    void* workspace, size_t workspace_bytes, int32_t* dev_status,
-                                    void* stream) {
-  if (!counts || !sums) return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: counts and sums are required");
-  if (B < 0 || N < 0 || K <= 0 || D <= 0)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: bad sizes");
+// fk_assign_accumulate and fk_assign_dot_accumulate: the method of
+// fk_assign_accumulate_method (privatised sum after the assignment, sums
+// fused into the assignment, or assignment then counting sort + segmented sum).
+static int assign_accumulate_entry(const char* fn, bool dot, const void* x, const void* centroids,
+                                   const void* x_sq, const void* c_sq, int32_t* out,
+                                   int32_t* counts, float* sums, int dtype, int xsq_dtype,
+                                   int csq_dtype, int64_t B, int64_t N, int64_t K, int64_t D,
+                                   const int64_t* x_strides3, const int64_t* c_strides3,
+                                   const int64_t* xsq_strides2, const int64_t* csq_strides2,
+                                   const int64_t* out_strides2, void* workspace,
+                                   size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (!counts || !sums) return fail(FK_ERR_INVALID_ARG, "%s: counts and sums are required", fn);
+  if (B < 0 || N < 0 || K <= 0 || D <= 0) return fail(FK_ERR_INVALID_ARG, "%s: bad sizes", fn);
   if (B == 0 || N == 0) return FK_OK;
   const size_t need = fk_assign_accumulate_workspace_size(B, N, K, D, dtype);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
-    return fail(FK_ERR_WORKSPACE, "fk_assign_accumulate: workspace needs %zu bytes, 256-aligned", need);
+    return fail(FK_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-aligned", fn, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto assign = [&](int32_t* cnt, size_t ws_bytes) {
+    return assign_entry(fn, dot, x, centroids, x_sq, c_sq, out, cnt, dtype, xsq_dtype, csq_dtype, B,
+                        N, K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2,
+                        workspace, ws_bytes, dev_status, stream);
+  };
   if (assign_accumulate_priv(K, D)) {
-    int st = fk_assign(x, centroids, x_sq, c_sq, out, nullptr, dtype, xsq_dtype, csq_dtype, B, N, K,
-                       D, x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2,
-                       workspace, workspace_bytes, dev_status, stream);
+    int st = assign(nullptr, workspace_bytes);
     if (st != FK_OK) return st;
     return segsum_priv(x, dtype, x_strides3, out, FK_I32, out_strides2, B, N, K, D, sums, counts,
                        dev_status, s);
@@ -1211,9 +1281,7 @@ extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const 
     void* wu = static_cast<uint8_t*>(workspace) + wa + align_up(static_cast<size_t>(B * K) * 4, 256);
     cudaError_t e = cudaMemsetAsync(hist, 0, static_cast<size_t>(B * K) * 4, s);
     if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    int st = fk_assign(x, centroids, x_sq, c_sq, out, hist, dtype, xsq_dtype, csq_dtype, B, N, K, D,
-                       x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2, workspace,
-                       wa, dev_status, stream);
+    int st = assign(hist, wa);
     if (st != FK_OK) return st;
     return fk_centroid_accumulate(x, dtype, B, N, K, D, x_strides3, out, FK_I32, out_strides2,
                                   hist, sums, counts, wu,
@@ -1221,17 +1289,17 @@ extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const 
                                   stream);
   }
   // fused path: same validation as fk_assign
-  if (!x || !centroids || !x_sq || !out || !x_strides3 || !c_strides3 || !xsq_strides2 ||
-      !out_strides2)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: null pointer argument");
-  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: c_sq without strides");
-  if (xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: x_sq dtype must be floating");
+  if (!x || !centroids || (!dot && !x_sq) || !out || !x_strides3 || !c_strides3 ||
+      (!dot && !xsq_strides2) || !out_strides2)
+    return fail(FK_ERR_INVALID_ARG, "%s: null pointer argument", fn);
+  if (c_sq && !csq_strides2) return fail(FK_ERR_INVALID_ARG, "%s: c_sq without strides", fn);
+  if (!dot && xsq_dtype != FK_F16 && xsq_dtype != FK_BF16 && xsq_dtype != FK_F32)
+    return fail(FK_ERR_INVALID_ARG, "%s: x_sq dtype must be floating", fn);
   if (c_sq && csq_dtype != FK_F16 && csq_dtype != FK_BF16 && csq_dtype != FK_F32)
-    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate: c_sq dtype must be floating");
-  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: K above 2^20");
+    return fail(FK_ERR_INVALID_ARG, "%s: c_sq dtype must be floating", fn);
+  if (K > (1 << 20)) return fail(FK_ERR_UNSUPPORTED, "%s: K above 2^20", fn);
   if (N >= (1ll << 31) || B * ((N + kRows - 1) / kRows) >= (1ll << 31))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: problem too large");
+    return fail(FK_ERR_UNSUPPORTED, "%s: problem too large", fn);
   const int64_t row_al = 8;
   int64_t xs[3] = {x_strides3[0], x_strides3[1], x_strides3[2]};
   int64_t cs[3] = {c_strides3[0], c_strides3[1], c_strides3[2]};
@@ -1240,16 +1308,42 @@ extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const 
   if (K == 1) cs[1] = (D + row_al - 1) / row_al * row_al;
   if (B == 1) { xs[0] = N * xs[1]; cs[0] = K * cs[1]; }
   if (!fk_tma_compatible(x, dtype, D, xs))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: x rows not TMA-addressable");
+    return fail(FK_ERR_UNSUPPORTED, "%s: x rows not TMA-addressable", fn);
   if (!fk_tma_compatible(centroids, dtype, D, cs))
-    return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate: centroid rows not TMA-addressable");
+    return fail(FK_ERR_UNSUPPORTED, "%s: centroid rows not TMA-addressable", fn);
   if (dtype == FK_F16)
     return assign_typed<__half>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N, K,
                                 D, xs, cs, xsq_strides2, csq_strides2, out_strides2, workspace,
-                                dev_status, s, sums);
+                                dev_status, s, sums, dot);
   return assign_typed<__nv_bfloat16>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B,
                                      N, K, D, xs, cs, xsq_strides2, csq_strides2, out_strides2,
-                                     workspace, dev_status, s, sums);
+                                     workspace, dev_status, s, sums, dot);
+}
+
+extern "C" int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq,
+                                    const void* c_sq, int32_t* out, int32_t* counts, float* sums,
+                                    int dtype, int xsq_dtype, int csq_dtype, int64_t B, int64_t N,
+                                    int64_t K, int64_t D, const int64_t* x_strides3,
+                                    const int64_t* c_strides3, const int64_t* xsq_strides2,
+                                    const int64_t* csq_strides2, const int64_t* out_strides2,
+                                    void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                    void* stream) {
+  return assign_accumulate_entry("fk_assign_accumulate", false, x, centroids, x_sq, c_sq, out,
+                                 counts, sums, dtype, xsq_dtype, csq_dtype, B, N, K, D, x_strides3,
+                                 c_strides3, xsq_strides2, csq_strides2, out_strides2, workspace,
+                                 workspace_bytes, dev_status, stream);
+}
+
+extern "C" int fk_assign_dot_accumulate(const void* x, const void* centroids, int32_t* out,
+                                        int32_t* counts, float* sums, int dtype, int64_t B,
+                                        int64_t N, int64_t K, int64_t D,
+                                        const int64_t* x_strides3, const int64_t* c_strides3,
+                                        const int64_t* out_strides2, void* workspace,
+                                        size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  return assign_accumulate_entry("fk_assign_dot_accumulate", true, x, centroids, nullptr, nullptr,
+                                 out, counts, sums, dtype, FK_F32, FK_F32, B, N, K, D, x_strides3,
+                                 c_strides3, nullptr, nullptr, out_strides2, workspace,
+                                 workspace_bytes, dev_status, stream);
 }
 
 // ---------------------------------------------------------------------------

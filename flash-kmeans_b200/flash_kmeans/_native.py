@@ -49,6 +49,8 @@ SIGNATURES = {
     "fk_assign": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL, _PL, _PL,
                        _PL, _P, _S, _P, _P]),
     "fk_assign_dot": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _L, _PL, _PL, _PL, _P, _S, _P, _P]),
+    "fk_assign_dot_accumulate": (_I, [_P, _P, _P, _P, _P, _I, _L, _L, _L, _L, _PL, _PL, _PL, _P,
+                                      _S, _P, _P]),
     "fk_assign_accumulate_workspace_size": (_S, [_L, _L, _L, _L, _I]),
     "fk_assign_accumulate_method": (_I, [_L, _L, _I]),
     "fk_assign_accumulate": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL,

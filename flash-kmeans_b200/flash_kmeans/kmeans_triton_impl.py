@@ -58,12 +58,7 @@ class LloydEngine:
         self.stat_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
         self.csq_valid = False
         lib = nat.load()
-        if metric == "euclid":
-            ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype))
-        else:  # fk_assign_dot, then fk_centroid_accumulate after it
-            self.ws_assign_bytes = lib.fk_assign_workspace_size(B, K, nat.dtype_code(dtype))
-            ws_bytes = -(-self.ws_assign_bytes // 256) * 256 + \
-                lib.fk_centroid_accumulate_workspace_size(B, N, K)
+        ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype))
         self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None
@@ -76,8 +71,8 @@ class LloydEngine:
         finalize; sorted -> c_sq staging, assignment, scan, scatter, segmented
         sum, finalize."""
         method = nat.load().fk_assign_accumulate_method(self.K, self.D, nat.dtype_code(self.dtype))
-        if self.metric == "dot":  # column mask, assignment, (privatised | sorted) sum, finalize
-            return 4 if method == nat.FK_ACC_PRIVATISED else 6
+        if self.metric == "dot":  # as below, without the c_sq staging
+            return {nat.FK_ACC_PRIVATISED: 3, nat.FK_ACC_FUSED: 2}.get(method, 5)
         return {nat.FK_ACC_PRIVATISED: 4, nat.FK_ACC_FUSED: 3}.get(method, 6)
 
     # ---------------------------------------------------------------- set-up
@@ -125,23 +120,17 @@ class LloydEngine:
         self.csq_valid = True
 
     def _step_dot(self, lib, s, status, ev_assign) -> None:
-        """Dot-product iteration: argmax assignment (labels and their counts),
-        per-cluster sums, L2-normalised means and the shift."""
+        """Dot-product iteration: argmax assignment with the per-cluster sums
+        and counts, then L2-normalised means and the shift."""
         B, N, K, D = self.B, self.N, self.K, self.D
         x = self.x
-        wa = self.ws_assign_bytes
-        ws_acc = self.ws[-(-wa // 256) * 256:]
         if ev_assign is not None:
             ev_assign[0].record()
-        nat.check(lib.fk_assign_dot(
+        nat.check(lib.fk_assign_dot_accumulate(
             nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.ids), nat.ptr(self.hist),
-            nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
-            nat.strides(self.ids, 2), nat.ptr(self.ws), wa, status, s), "fk_assign_dot")
-        nat.check(lib.fk_centroid_accumulate(
-            nat.ptr(x), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3), nat.ptr(self.ids),
-            nat.FK_I32, nat.strides(self.ids, 2), nat.ptr(self.hist), nat.ptr(self.sums),
-            nat.ptr(self.hist), nat.ptr(ws_acc), ws_acc.numel(), status, s),
-            "fk_centroid_accumulate")
+            nat.ptr(self.sums), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3),
+            nat.strides(self.c_cur, 3), nat.strides(self.ids, 2), nat.ptr(self.ws), self.ws.numel(),
+            status, s), "fk_assign_dot_accumulate")
         if ev_assign is not None:
             ev_assign[1].record()
         nat.check(lib.fk_centroid_finalize_normalized(

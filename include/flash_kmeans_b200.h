@@ -34,6 +34,10 @@
  *   fk_assign_dot          <- cosine_assign_triton, flash_kmeans/assign_euclid_triton.py:1415-1498
  *                             (kernels _cosine_assign_kernel :1038-1131 and its split-D
  *                             variant :1137-1231), used by batch_kmeans_Cosine / _Dot
+ *   fk_assign_dot_accumulate
+ *                          <- cosine_assign_triton + the accumulate phase of
+ *                             triton_centroid_update_sorted_cosine, as paired in
+ *                             _cosine_iter / _dot_iter, kmeans_triton_impl.py:19-35
  *   fk_row_normalize       <- F.normalize of x in batch_kmeans_Cosine,
  *                             flash_kmeans/kmeans_triton_impl.py:135
  *   fk_centroid_finalize_normalized
@@ -157,6 +161,20 @@ int fk_assign_accumulate(const void* x, const void* centroids, const void* x_sq,
                          const int64_t* xsq_strides2, const int64_t* csq_strides2,
                          const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
                          int32_t* dev_status, void* stream);
+
+/* fk_assign_dot fused with the accumulation of one cosine / dot-product Lloyd
+ * iteration (replaces cosine_assign_triton + the accumulate phase of
+ * triton_centroid_update_sorted_cosine in _cosine_iter / _dot_iter,
+ * flash_kmeans/kmeans_triton_impl.py:19-35).  Arguments as fk_assign_dot
+ * plus `sums`; `counts` is required; sums and counts are ADDED to, by the
+ * method fk_assign_accumulate_method names; workspace
+ * fk_assign_accumulate_workspace_size.  Follow with
+ * fk_centroid_finalize_normalized. */
+int fk_assign_dot_accumulate(const void* x, const void* centroids, int32_t* out, int32_t* counts,
+                             float* sums, int dtype, int64_t B, int64_t N, int64_t K, int64_t D,
+                             const int64_t* x_strides3, const int64_t* c_strides3,
+                             const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
+                             int32_t* dev_status, void* stream);
 
 /* fk_assign for callers that cannot allocate (no counterpart in the reference).
  * Some hosts give a plugin only its inputs and outputs: a serving framework's
