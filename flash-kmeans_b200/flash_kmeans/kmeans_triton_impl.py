@@ -28,6 +28,11 @@ def _round_tol(tol: float, dtype: torch.dtype) -> float:
     return float(torch.tensor(float(tol), dtype=dtype))
 
 
+# Runs of at least this many iterations replay their steps from CUDA graphs:
+# capture costs about as much host time as 50 eager steps save.
+_GRAPH_MIN_ITERS = 64
+
+
 class LloydEngine:
     """Buffers and launches for batched Lloyd iterations on one device.
 
@@ -37,10 +42,12 @@ class LloydEngine:
     """
 
     def __init__(self, B: int, N: int, K: int, D: int, dtype: torch.dtype, device,
-                 metric: str = "euclid"):
+                 metric: str = "euclid", use_graphs: bool = True):
         """``metric``: "euclid" (nearest centroid, mean update) or "dot"
         (largest dot product, L2-normalised mean update: the cosine and
-        dot-product k-means of the reference)."""
+        dot-product k-means of the reference).  ``use_graphs``: replay the
+        steady-state step as CUDA graphs (see ``step``); capturing the two
+        pairs costs about 1.5 ms, so it pays for long runs only."""
         if metric not in ("euclid", "dot"):
             raise ValueError(f"unknown metric {metric!r}")
         self.metric = metric
@@ -62,6 +69,11 @@ class LloydEngine:
         self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None
+        self.use_graphs = use_graphs
+        self._graphs = {}
+        self._arg_cache = {}
+        self._capture_stream = None
+        self._steps = 0
 
     @property
     def kernels_per_step(self) -> int:
@@ -82,6 +94,9 @@ class LloydEngine:
             self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
         self.c_cur.copy_(centroids.view(self.B, self.K, self.D))
         self.csq_valid = False
+        self._graphs.clear()   # captured with the previous x
+        self._arg_cache.clear()
+        self._steps = 0
         self.stat.zero_()
         self.hist.zero_()
         self.sums.zero_()
@@ -91,53 +106,121 @@ class LloydEngine:
         """One Lloyd iteration: ids <- assign(centroids); c_nxt <- update; shift.
 
         ``ev_assign``: optional (start, end) CUDA events recorded around the
-        assignment (with its fused accumulation) on the current stream."""
-        lib = nat.load()
-        B, N, K, D = self.B, self.N, self.K, self.D
-        x, dev = self.x, self.device
-        s = nat.stream_handle(dev)
-        status = nat.ptr(self.stat[1:2])
-        if self.metric == "dot":
-            self._step_dot(lib, s, status, ev_assign)
-            return
-        c_sq = self.csq if self.csq_valid else None
+        assignment (with its accumulation) on the current stream.
+
+        From the second step on (the first one stages c_sq from the centroids
+        and sets the kernels' shared-memory attributes) the two launches of a
+        step replay as CUDA graphs, one pair per centroid buffer, so a step
+        costs two graph launches on the host instead of argument marshalling,
+        tensor-map encoding and three to six kernel launches."""
+        # a caller that overwrote c_cur clears csq_valid: the Euclidean graph
+        # would pass the stale c_sq, so that step runs eagerly
+        if self.use_graphs and self._steps > 0 and (self.metric == "dot" or self.csq_valid):
+            pair = self._graph_pair()
+            if pair is not None:
+                if ev_assign is not None:
+                    ev_assign[0].record()
+                pair[0].replay()
+                if ev_assign is not None:
+                    ev_assign[1].record()
+                pair[1].replay()
+                self._steps += 1
+                return
         if ev_assign is not None:
             ev_assign[0].record()
-        nat.check(lib.fk_assign_accumulate(
-            nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.x_sq), nat.ptr(c_sq), nat.ptr(self.ids),
-            nat.ptr(self.hist), nat.ptr(self.sums), nat.dtype_code(x.dtype),
-            nat.dtype_code(self.x_sq.dtype), nat.FK_F32, B, N, K, D, nat.strides(x, 3),
-            nat.strides(self.c_cur, 3), nat.strides(self.x_sq, 2), nat.strides(self.csq, 2),
-            nat.strides(self.ids, 2), nat.ptr(self.ws), self.ws.numel(), status, s),
-            "fk_assign_accumulate")
+        self._launch_assign()
         if ev_assign is not None:
             ev_assign[1].record()
-        nat.check(lib.fk_centroid_finalize(
-            nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
-            nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
-            nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 1, s),
-            "fk_centroid_finalize")
+        self._launch_finalize()
         self.csq_valid = True
+        self._steps += 1
 
-    def _step_dot(self, lib, s, status, ev_assign) -> None:
-        """Dot-product iteration: argmax assignment with the per-cluster sums
-        and counts, then L2-normalised means and the shift."""
+    def _launch_assign(self) -> None:
+        """Assignment with the per-cluster sums and counts, on the current stream."""
+        lib = nat.load()
+        s = nat.stream_handle(self.device)
+        if self.metric == "dot":
+            nat.check(lib.fk_assign_dot_accumulate(*self._args("assign"), s),
+                      "fk_assign_dot_accumulate")
+        else:
+            nat.check(lib.fk_assign_accumulate(*self._args("assign"), s), "fk_assign_accumulate")
+
+    def _launch_finalize(self) -> None:
+        """New centroids, shift (and the next c_sq), accumulators reset."""
+        lib = nat.load()
+        s = nat.stream_handle(self.device)
+        if self.metric == "dot":
+            nat.check(lib.fk_centroid_finalize_normalized(*self._args("finalize"), s),
+                      "fk_centroid_finalize_normalized")
+        else:
+            nat.check(lib.fk_centroid_finalize(*self._args("finalize"), s), "fk_centroid_finalize")
+
+    def _args(self, which: str) -> tuple:
+        """ctypes arguments (all but the stream) of this step's calls, built
+        once per centroid buffer and c_sq state: marshalling them costs more
+        host time than the launches themselves."""
+        c_sq_on = self.metric == "euclid" and self.csq_valid
+        key = (which, self.c_cur.data_ptr(), c_sq_on)
+        a = self._arg_cache.get(key)
+        if a is not None:
+            return a
         B, N, K, D = self.B, self.N, self.K, self.D
         x = self.x
-        if ev_assign is not None:
-            ev_assign[0].record()
-        nat.check(lib.fk_assign_dot_accumulate(
-            nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.ids), nat.ptr(self.hist),
-            nat.ptr(self.sums), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3),
-            nat.strides(self.c_cur, 3), nat.strides(self.ids, 2), nat.ptr(self.ws), self.ws.numel(),
-            status, s), "fk_assign_dot_accumulate")
-        if ev_assign is not None:
-            ev_assign[1].record()
-        nat.check(lib.fk_centroid_finalize_normalized(
-            nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
-            nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
-            nat.strides(self.c_nxt, 3), nat.ptr(self.stat[0:1]), 1, s),
-            "fk_centroid_finalize_normalized")
+        status = nat.ptr(self.stat[1:2])
+        if which == "assign" and self.metric == "dot":
+            a = (nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.ids), nat.ptr(self.hist),
+                 nat.ptr(self.sums), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3),
+                 nat.strides(self.c_cur, 3), nat.strides(self.ids, 2), nat.ptr(self.ws),
+                 self.ws.numel(), status)
+        elif which == "assign":
+            a = (nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.x_sq),
+                 nat.ptr(self.csq if c_sq_on else None), nat.ptr(self.ids), nat.ptr(self.hist),
+                 nat.ptr(self.sums), nat.dtype_code(x.dtype), nat.dtype_code(self.x_sq.dtype),
+                 nat.FK_F32, B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
+                 nat.strides(self.x_sq, 2), nat.strides(self.csq, 2), nat.strides(self.ids, 2),
+                 nat.ptr(self.ws), self.ws.numel(), status)
+        elif self.metric == "dot":
+            a = (nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
+                 nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
+                 nat.strides(self.c_nxt, 3), nat.ptr(self.stat[0:1]), 1)
+        else:
+            a = (nat.ptr(self.sums), nat.ptr(self.hist), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
+                 nat.dtype_code(self.dtype), B, K, D, nat.strides(self.c_cur, 3),
+                 nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 1)
+        self._arg_cache[key] = a
+        return a
+
+    def _graph_pair(self):
+        """(assignment, finalize) graphs for the current centroid buffer,
+        captured on first use; None (eager from then on) if capture fails."""
+        key = self.c_cur.data_ptr()
+        pair = self._graphs.get(key)
+        if pair is not None:
+            return pair
+        cur = torch.cuda.current_stream(self.device)
+        side = self._capture_stream
+        if side is None:
+            side = self._capture_stream = torch.cuda.Stream(self.device)
+        side.wait_stream(cur)
+        try:
+            pair = []
+            with torch.cuda.stream(side):
+                for launch in (self._launch_assign, self._launch_finalize):
+                    g = torch.cuda.CUDAGraph()
+                    g.capture_begin()
+                    try:
+                        launch()
+                    finally:
+                        g.capture_end()
+                    pair.append(g)
+        except RuntimeError:
+            self.use_graphs = False
+            self._graphs.clear()
+            cur.wait_stream(side)
+            return None
+        cur.wait_stream(side)
+        self._graphs[key] = pair
+        return pair
 
     def advance(self) -> None:
         """Adopt the updated centroids for the next iteration."""
@@ -197,7 +280,7 @@ def batch_kmeans_Euclid(
     centroids = centroids.view(B, K, D)
 
     with torch.cuda.device(x.device):
-        eng = LloydEngine(B, N, K, D, x.dtype, x.device)
+        eng = LloydEngine(B, N, K, D, x.dtype, x.device, use_graphs=max_iters >= _GRAPH_MIN_ITERS)
         eng.load(x, centroids)
         need_sync = tol > 0 or verbose
         tol_r = _round_tol(tol, x.dtype)
@@ -236,7 +319,8 @@ def _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verb
         centroids = centroids.view(B, K, D)
         if cosine:
             centroids = _ops.row_normalize(centroids)
-        eng = LloydEngine(B, N, K, D, x.dtype, x.device, metric="dot")
+        eng = LloydEngine(B, N, K, D, x.dtype, x.device, metric="dot",
+                          use_graphs=max_iters >= _GRAPH_MIN_ITERS)
         eng.load(xs, centroids)
         need_sync = tol > 0 or verbose
         tol_r = _round_tol(tol, x.dtype)

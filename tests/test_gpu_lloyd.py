@@ -214,3 +214,38 @@ def test_kmeans_largeN_tol_break_returns_new_centroids(fk):
     # ... and the run had converged: one more assignment barely moves anything
     again = ko.assign(x[None], _np(cent)[None], ko.row_sqnorm(x[None], "float32"), "float32")[0]
     assert (again == lab).mean() > 0.999
+
+
+@pytest.mark.parametrize("metric,dt,K,D", [("euclid", "float16", 1000, 128),   # fused
+                                           ("euclid", "float32", 700, 96),     # sorted
+                                           ("euclid", "bfloat16", 64, 64),     # privatised
+                                           ("dot", "float16", 1000, 128)])
+def test_engine_graph_replay_matches_eager(fk, metric, dt, K, D):
+    """Steps replayed from CUDA graphs give the eager steps' labels and
+    centroids (well-separated clusters, so float-atomic order cannot flip a
+    label), and the graphs are really used."""
+    from flash_kmeans import _ops
+    from flash_kmeans.kmeans_triton_impl import LloydEngine
+    rng = np.random.default_rng(77)
+    B, N = 2, 6000
+    x = ko.round_to(ko.gmm_points(rng, B, N, D, K, 8.0), dt)
+    c0 = ko.init_from_points(rng, x, K, replace=False)
+    xd, cd = _dev(x, dt), _dev(c0, dt)
+    if metric == "dot":
+        xd, cd = _ops.row_normalize(xd), _ops.row_normalize(cd)
+    out = []
+    for graphs in (False, True):
+        eng = LloydEngine(B, N, K, D, TD[dt], "cuda", metric=metric, use_graphs=graphs)
+        eng.load(xd, cd)
+        shifts = []
+        for _ in range(5):
+            eng.step()
+            shifts.append(eng.read_stat())
+            eng.advance()
+        assert all(code == 0 for _, code in shifts)
+        out.append((eng.ids.cpu().numpy(), _np(eng.result_centroids()), [sh for sh, _ in shifts]))
+        if graphs:
+            assert eng.use_graphs and len(eng._graphs) == 2
+    np.testing.assert_array_equal(out[0][0], out[1][0])
+    assert_centroids(out[1][1], out[0][1], "graph vs eager", rtol=1e-5)
+    np.testing.assert_allclose(out[1][2], out[0][2], rtol=1e-3, atol=1e-6)

@@ -292,7 +292,9 @@ def test_cosine_engine_launch_count_and_no_allocation(fk):
     eng = LloydEngine(B, N, K, D, torch.float16, "cuda", metric="dot")
     assert eng.kernels_per_step in (2, 3, 5)  # fused, privatised, sorted
     eng.load(x, x[:, :K])
-    eng.step()
+    for _ in range(3):   # eager first step, then the graphs of both centroid buffers
+        eng.step()
+        eng.advance()
     torch.cuda.synchronize()
     before = torch.cuda.memory_stats()["allocation.all.allocated"]
     for _ in range(3):
