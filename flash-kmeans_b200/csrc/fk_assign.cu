@@ -684,9 +684,12 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       // load, so at most one is outstanding); a centroid tile's accumulator
       // is released as soon as its last chunk is in registers.
       // 16-byte c_sq words per chunk prefetched with the TMEM load (packed
-      // 16-bit mode only; the float32-chain modes load theirs when reducing,
-      // their register budget has no room for a second set)
-      constexpr int kCsqVec = (MODE == 0) ? 4 : 1;
+      // 16-bit mode without fused sums).  The float32-chain modes load theirs
+      // when reducing, and so does the fused kernel: its 14 warps leave 128
+      // registers per thread, where the two prefetch sets spilled (0.86 ->
+      // 0.79 ms at B=32, N=75600, K=1000, D=128 without them).
+      constexpr bool kCsqPrefetch = MODE == 0 && !FUSE;
+      constexpr int kCsqVec = kCsqPrefetch ? 4 : 1;
       static_assert(kGChunks % 2 == 0, "chunks per group must be even");
       const int nchunks = p.nkt * kGChunks;
       uint32_t va[32], vb[32];
@@ -703,7 +706,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                       static_cast<uint32_t>(ab * kCent + h * kGCols + ch * 32),
                   v);
-        if constexpr (MODE == 0) {
+        if constexpr (kCsqPrefetch) {
           const int col0 = (g / kGChunks) * kCent + h * kGCols + ch * 32;
           const uint4* src = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
 #pragma unroll
@@ -722,8 +725,14 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       };
       auto reduce = [&](int g, uint32_t(&v)[32], const uint4(&cq)[kCsqVec]) {
         const int col0 = (g / kGChunks) * kCent + h * kGCols + (g % kGChunks) * 32;
-        if constexpr (MODE == 0) {
+        if constexpr (kCsqPrefetch) {
           am.chunk32(v, reinterpret_cast<const uint32_t*>(cq), xsq2, col0);
+        } else if constexpr (MODE == 0) {
+          const uint4* src = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
+          uint4 c4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) c4[i] = __ldg(src + i);
+          am.chunk32(v, reinterpret_cast<const uint32_t*>(c4), xsq2, col0);
         } else if constexpr (MODE >= 3) {
           am.chunk32(v, col0, p.K);
         } else {

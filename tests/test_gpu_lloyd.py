@@ -248,4 +248,6 @@ def test_engine_graph_replay_matches_eager(fk, metric, dt, K, D):
             assert eng.use_graphs and len(eng._graphs) == 2
     np.testing.assert_array_equal(out[0][0], out[1][0])
     assert_centroids(out[1][1], out[0][1], "graph vs eager", rtol=1e-5)
-    np.testing.assert_allclose(out[1][2], out[0][2], rtol=1e-3, atol=1e-6)
+    # once converged the shift is float-atomic-order noise: compare on the
+    # scale of the first shift
+    np.testing.assert_allclose(out[1][2], out[0][2], rtol=1e-3, atol=1e-5 * max(out[0][2]))
