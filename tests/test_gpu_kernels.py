@@ -249,7 +249,11 @@ def test_accumulate_privatised_and_sorted_paths(fk, dt, B, N, K, D, idt):
     ("float16", 3, 5000, 1000, 128), ("float16", 2, 700, 70, 64), ("bfloat16", 2, 900, 33, 100),
     ("float16", 1, 1000, 50, 17), ("float16", 1, 640, 40, 192), ("float32", 2, 800, 60, 48),
     ("bfloat16", 2, 900, 600, 100), ("float16", 1, 3000, 3100, 17), ("float16", 1, 640, 300, 192),
-    ("float32", 1, 1200, 1100, 48)])
+    ("float32", 1, 1200, 1100, 48),
+    # CTA ranges that cross many batch boundaries, one long batch with K = 128, K = 1,
+    # and float32 x_sq (mode 1)
+    ("float16", 64, 1000, 100, 128), ("bfloat16", 40, 700, 17, 64),
+    ("float16", 1, 300000, 128, 128), ("float16", 3, 129, 1, 8), ("float16-xsq32", 5, 3000, 60, 128)])
 def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     """fk_assign_accumulate (privatised for small K x D, fused for 16-bit D<=128, sorted
     otherwise) equals fk_assign + torch index_add: labels bit-identical, counts exact, sums
@@ -257,10 +261,12 @@ def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     from flash_kmeans import _native as nat
     from flash_kmeans import _ops
     lib = nat.load()
-    rng = np.random.default_rng(B * 7 + D)
+    xsq32 = dt.endswith("-xsq32")
+    dt = dt.replace("-xsq32", "")
+    rng = np.random.default_rng(B * 7 + D + K)
     x = _ops.ensure_tma(_dev(ko.round_to(rng.standard_normal((B, N, D), dtype=np.float32), dt), dt))
     c = _ops.ensure_tma(_dev(ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt), dt))
-    xsq = _ops.row_sqnorm(x)
+    xsq = (x.float() ** 2).sum(-1) if xsq32 else _ops.row_sqnorm(x)
     ref = _ops.assign(x, c, xsq)
     ref_s, ref_c = _torch_sums(x, ref, K)
     out = torch.full((B, N), -1, dtype=torch.int32, device="cuda")

@@ -114,7 +114,10 @@ def test_random_init_uses_cuda_rng_like_reference(fk):
     idx = torch.randint(0, 4096, (2, 32), device="cuda")
     c0 = torch.gather(x, 1, idx[..., None].expand(-1, -1, 64))
     ids2, cent2, _ = fk.batch_kmeans_Euclid(x, 32, max_iters=1, init_centroids=c0)
-    assert torch.equal(ids, ids2) and torch.equal(cent, cent2)
+    # the same initial centroids; the cluster sums are float atomics whose order
+    # varies between runs, so the centroids agree to rounding, not bit for bit
+    assert (ids == ids2).float().mean().item() >= 0.999
+    torch.testing.assert_close(cent.float(), cent2.float(), rtol=2e-3, atol=2e-3)
 
 
 def test_flashkmeans_api_matches_raw(fk):

@@ -279,7 +279,10 @@ def test_cosine_random_init_uses_cuda_rng_like_reference(fk):
     idx = torch.randint(0, 4096, (2, 32), device="cuda")
     c0 = torch.gather(_ops.row_normalize(x), 1, idx[..., None].expand(-1, -1, 64))
     ids2, cent2, _ = fk.batch_kmeans_Cosine(x, 32, max_iters=2, init_centroids=c0)
-    assert torch.equal(ids, ids2) and torch.equal(cent, cent2)
+    # the same initial centroids; the cluster sums are float atomics whose order
+    # varies between runs, so the centroids agree to rounding, not bit for bit
+    assert (ids == ids2).float().mean().item() >= 0.999
+    torch.testing.assert_close(cent.float(), cent2.float(), rtol=2e-3, atol=2e-3)
 
 
 def test_cosine_engine_launch_count_and_no_allocation(fk):
@@ -308,7 +311,9 @@ def test_cosine_engine_launch_count_and_no_allocation(fk):
     ("float16", 2, 20000, 1000, 128),    # fused sums in the assignment kernel
     ("bfloat16", 1, 30000, 1000, 64),    # fused, D = 64
     ("float16", 3, 9000, 128, 128),      # privatised sum, narrow tiles
-    ("bfloat16", 1, 7000, 50, 100),      # privatised, split-D
+    ("bfloat16", 1, 7000, 50, 100),      # privatised, D = 100
+    ("float16", 50, 900, 64, 64),        # privatised, many batches
+    ("float16", 1, 3000, 200, 192),      # privatised, split-D
     ("float16", 1, 5000, 2000, 192),     # sorted (D > 128)
     ("float32", 2, 4000, 700, 96),       # sorted, float32
     ("float32", 1, 3000, 40, 64),        # privatised, float32
