@@ -768,8 +768,15 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
           }
       };
       if constexpr (STAGED) {
-        // batches of RB rows (one 2 KB buffer) in sorted order; batch b+1's
-        // copies are in flight while batch b is summed from shared memory
+        // Batches of RB rows (one 2 KB buffer) in sorted order; batch b+1's
+        // copies are in flight while batch b is summed from shared memory.
+        // The chunk is in label order, so a row's label follows from the
+        // run bounds (start[] of the scan): one label lookup per run, none
+        // per row, and four rows' loads issued before their adds.  A run
+        // wholly inside this warp's range [q0, q1) belongs to no other warp
+        // in this chunk and is flushed with plain read-add-writes; only the
+        // first and last run, which a neighbour may share, use atomics
+        // (shared float atomics cost about 70 cycles each).
         const int rowb = D * static_cast<int>(sizeof(T));
         const int RB = kPrivStageBuf / rowb;
         uint8_t* wst = wstage + static_cast<size_t>(warp) * 2 * kPrivStageBuf;
@@ -786,6 +793,27 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
           }
           cp_async_commit();
         };
+        auto run_end = [&](int k) { return k + 1 < K ? start[k + 1] : nv; };
+        int bound = 0;
+        if (q0 < q1) {
+          cur = slab[perm[q0]];
+          bound = run_end(cur);
+        }
+        auto flush_run = [&]() {
+          float* dst = ssum + cur * R + lane;
+          const bool own = start[cur] >= q0 && bound <= q1;
+#pragma unroll
+          for (int g = 0; g < NG; ++g)
+            if (g * 128 + lane * 4 < D) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float* w = dst + g * 128 + 32 * e;
+                if (own) *w += acc[g][e];
+                else atomicAdd(w, acc[g][e]);
+                acc[g][e] = 0.f;
+              }
+            }
+        };
         if (q0 < q1) issue(q0, 0);
         int buf = 0;
         for (int qb = q0; qb < q1; qb += RB, buf ^= 1) {
@@ -794,27 +822,43 @@ __global__ void __launch_bounds__(kPrivThreads) segsum_priv_kernel(
           cp_async_wait<1>();      // batch qb has landed (this lane's copies)
           __syncwarp();            // ... and every lane's
           const uint8_t* rows = wst + buf * kPrivStageBuf;
-          for (int rr = 0; rr < RB && qb + rr < q1; ++rr) {
-            const int lab = slab[perm[qb + rr]];
-            if (lab != cur) {
-              if (cur >= 0) flush();
-              cur = lab;
-            }
-            const T* row = reinterpret_cast<const T*>(rows + rr * rowb);
+          const int nr = min(RB, q1 - qb);
+          for (int r0 = 0; r0 < nr; r0 += 4) {
+            float f[4][NG][4];
 #pragma unroll
-            for (int g = 0; g < NG; ++g) {
-              const int d = g * 128 + lane * 4;
-              if (d < D) {
-                float f[4];
-                load4_f<T>(row, d, D, 1, true, f);
+            for (int u = 0; u < 4; ++u) {
+              const T* row = reinterpret_cast<const T*>(rows + (r0 + u) * rowb);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[g][e] += f[e];
+              for (int g = 0; g < NG; ++g) {
+                const int d = g * 128 + lane * 4;
+                if (r0 + u < nr && d < D) {
+                  load4_f<T>(row, d, D, 1, true, f[u][g]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) f[u][g][e] = 0.f;
+                }
               }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int q = qb + r0 + u;
+              if (r0 + u >= nr) break;
+              if (q >= bound) {  // the run ended before q: flush it, enter q's run
+                flush_run();
+                cur = slab[perm[q]];
+                bound = run_end(cur);
+              }
+#pragma unroll
+              for (int g = 0; g < NG; ++g)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[g][e] += f[u][g][e];
             }
           }
           __syncwarp();  // the buffer is refilled two steps later
         }
         cp_async_wait<0>();
+        if (cur >= 0) flush_run();
+        cur = -1;
       } else {
       // rows loaded per warp before summing (more would lower occupancy)
       constexpr int kB = 4;
