@@ -588,7 +588,7 @@ static int hist_scatter(const void* ids, const int64_t* is, int64_t B, int64_t N
 // (column 4i+e at slot 32e+i) so a warp's flush touches 32 consecutive words
 // per instruction.
 constexpr int kPrivThreads = 512;
-constexpr int kPrivChunk = 2048;
+constexpr int kPrivChunk = 4096;
 constexpr size_t kPrivMaxSmem = 200 * 1024;
 static_assert(kPrivChunk % kPrivThreads == 0, "chunk must be a multiple of the block");
 
