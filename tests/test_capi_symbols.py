@@ -69,3 +69,41 @@ def test_invalid_arguments_fail_on_host(lib):
     rc = lib.fk_centroid_accumulate(None, 0, 1, 1, 4, 8, st, None, 3, st, None, None, None, None,
                                     0, None, None)
     assert rc == 1
+
+
+def test_similarity_entry_points_validate_on_host(lib):
+    """The cosine / dot-product entry points reject bad calls before any CUDA call."""
+    st3 = (ctypes.c_int64 * 3)(1, 1, 1)
+    st2 = (ctypes.c_int64 * 2)(1, 1)
+    # K = 0, then null pointers with valid sizes
+    assert lib.fk_assign_dot(None, None, None, None, 0, 1, 4, 0, 8, st3, st3, st2, None, 0, None,
+                             None) == 1
+    assert b"bad sizes" in lib.fk_last_error()
+    assert lib.fk_assign_dot(None, None, None, None, 0, 1, 4, 2, 8, st3, st3, st2, None, 0, None,
+                             None) == 1
+    assert b"null pointer" in lib.fk_last_error()
+    # the fused variant needs counts and sums
+    assert lib.fk_assign_dot_accumulate(None, None, None, None, None, 0, 1, 4, 2, 8, st3, st3, st2,
+                                        None, 0, None, None) == 1
+    assert b"counts and sums" in lib.fk_last_error()
+    assert lib.fk_row_normalize(None, 0, 1, 4, 0, st3, None, st3, None) == 1
+    assert lib.fk_row_normalize(None, 0, 1, 4, 8, st3, None, st3, None) == 1
+    assert b"null pointer" in lib.fk_last_error()
+    assert lib.fk_row_normalize(ctypes.c_void_p(16), 0, 1, 1 << 31, 8, st3, ctypes.c_void_p(16),
+                                st3, None) == 2   # unsupported: N >= 2^31
+    # finalize: K = 0, null pointers, and new aliasing old
+    assert lib.fk_centroid_finalize_normalized(None, None, None, None, 0, 1, 0, 8, st3, st3, None, 0,
+                                               None) == 1
+    assert lib.fk_centroid_finalize_normalized(None, None, None, None, 0, 1, 2, 8, st3, st3, None, 0,
+                                               None) == 1
+    p = ctypes.c_void_p(256)
+    assert lib.fk_centroid_finalize_normalized(p, p, p, p, 0, 1, 2, 8, st3, st3, None, 0, None) == 1
+    assert b"aliases" in lib.fk_last_error()
+
+
+def test_accumulate_method_codes_are_stable(lib):
+    from flash_kmeans import _native
+    assert (_native.FK_ACC_PRIVATISED, _native.FK_ACC_FUSED, _native.FK_ACC_SORTED) == (0, 1, 2)
+    assert lib.fk_assign_accumulate_method(128, 128, 0) == _native.FK_ACC_PRIVATISED
+    assert lib.fk_assign_accumulate_method(1000, 128, 0) == _native.FK_ACC_FUSED
+    assert lib.fk_assign_accumulate_method(1024, 2048, 2) == _native.FK_ACC_SORTED
