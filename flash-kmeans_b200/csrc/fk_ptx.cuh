@@ -99,8 +99,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
-// 3-D tiled bulk tensor load global -> this CTA's shared memory, completion
-// reported as transaction bytes on `bar`.  No cluster multicast.
+// 3-D tiled bulk tensor load global -> this CTA's shared memory only,
+// completion reported as transaction bytes on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2) {
   asm volatile(
@@ -110,7 +110,7 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-// Untiled bulk copy global -> this CTA's shared memory (no cluster multicast).
+// Untiled bulk copy global -> this CTA's shared memory only.
 // Both addresses 16-byte aligned, `bytes` a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
                                           uint64_t* bar) {
