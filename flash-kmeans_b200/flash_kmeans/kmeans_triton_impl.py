@@ -207,7 +207,10 @@ class LloydEngine:
             with torch.cuda.stream(side):
                 for launch in (self._launch_assign, self._launch_finalize):
                     g = torch.cuda.CUDAGraph()
-                    g.capture_begin()
+                    # thread-local: the capture restricts only this thread's
+                    # CUDA calls (kernel launches and memsets here), not those
+                    # of other threads such as a communicator's
+                    g.capture_begin(capture_error_mode="thread_local")
                     try:
                         launch()
                     finally:
