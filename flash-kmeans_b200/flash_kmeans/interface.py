@@ -1,9 +1,11 @@
 """sklearn/faiss-style facade, drop-in for flash_kmeans.interface.FlashKMeans.
 
 Routing follows the reference (interface.py:106-262): host-resident data with
-more than ``chunk_size_data_cpu`` points (2-D only) goes through the
-out-of-core ``kmeans_largeN`` path; everything else is moved to ``device`` in
-the compute dtype and clustered by ``batch_kmeans_Euclid``.  This build has no
+more than ``chunk_size_data_cpu`` points goes through the out-of-core
+``kmeans_largeN`` path; everything else is moved to ``device`` in the compute
+dtype and clustered by ``batch_kmeans_Euclid``.  Batched (B, N, D) host data
+takes the out-of-core path too (the reference asserts it unsupported,
+interface.py:138 and :225; ``kmeans_largeN`` here takes batched input).  This build has no
 PyTorch/CPU fallback: ``use_triton=False`` or a machine without CUDA raises a
 RuntimeError at ``train``/``predict`` time instead of silently switching paths.
 """
@@ -92,9 +94,10 @@ class FlashKMeans:
         torch.cuda.manual_seed_all(self.seed)
 
         if data.device.type == "cpu" and N > self.chunk_size_data_cpu:
-            assert B is None, "Batched data with large N on CPU is not supported yet."
+            # 2-D data goes in as (N, D), so the random init draws exactly what
+            # the reference's kmeans_largeN draws for the same seed
             cluster_ids_b, centroids_b = kmeans_largeN(
-                x_b[0],
+                x_b if B is not None else data,
                 self.k,
                 max_iters=self.niter,
                 tol=self.tol,
@@ -103,8 +106,8 @@ class FlashKMeans:
                 BLOCK_N=self.chunk_size_data_cpu,
                 device=self._raw_device,
             )
-            centroids_b = centroids_b.unsqueeze(0)
-            cluster_ids_b = cluster_ids_b.unsqueeze(0)
+            if B is None:
+                cluster_ids_b, centroids_b = cluster_ids_b.unsqueeze(0), centroids_b.unsqueeze(0)
         else:
             compute_dtype = self.dtype or x_b.dtype
             x_b = x_b.to(device=self.device, dtype=compute_dtype, copy=False)
@@ -136,14 +139,14 @@ class FlashKMeans:
                 f"but predict received B={B}. Provide matching batch size.")
         _require_cuda(self.use_triton)
         if data.device.type == "cpu" and N > self.chunk_size_data_cpu:
-            assert B is None, "Batched data with large N on CPU is not supported yet."
-            return kmeans_largeN_assign(
-                x_b[0],
-                self.centroids_b[0],
+            labels_b = kmeans_largeN_assign(
+                x_b,
+                self.centroids_b,
                 dtype=self.dtype,
                 BLOCK_N=self.chunk_size_data_cpu,
                 device=self._raw_device,
             )
+            return labels_b.squeeze(0) if B is None else labels_b
         compute_dtype = self.dtype or x_b.dtype
         x_b = x_b.to(device=self.device, dtype=compute_dtype, copy=False)
         cent = self.centroids_b.to(device=x_b.device, dtype=compute_dtype)

@@ -25,7 +25,10 @@ B200 design:
 * reduction: every device ends with identical sums/counts after an NCCL
   all-reduce (single-process communicator over the devices, or the process
   group when one process drives one GPU), then finalizes its own replica, so
-  no broadcast is needed.
+  no broadcast is needed;
+* batched input (B, N, D) (an extension: the reference asserts it away,
+  interface.py:138): the B independent problems share the block pipeline,
+  each block carrying the same point range of every batch.
 """
 from __future__ import annotations
 
@@ -64,8 +67,8 @@ def partition_blocks(N: int, BLOCK_N: int, G: int):
 
 
 def _fits_resident(dev, rows: int, D: int, dtype: torch.dtype) -> bool:
-    """Whether `rows` rows of x (padded like the block buffers) take at most
-    half of the device's free memory."""
+    """Whether `rows` rows of x (padded like the block buffers; all batches'
+    rows counted) take at most half of the device's free memory."""
     esize = torch.empty((), dtype=dtype).element_size()
     row_bytes = -(-D * esize // 16) * 16
     free, _ = torch.cuda.mem_get_info(dev)
@@ -75,12 +78,14 @@ def _fits_resident(dev, rows: int, D: int, dtype: torch.dtype) -> bool:
 class _DeviceLane:
     """Per-device streaming pipeline for one contiguous slice of x.
 
-    ``resident``: copy every block once into one device buffer and reuse it
-    on later passes (no per-pass host transfers)."""
+    ``x_host`` is (B, N, D); every block holds the same point range of all B
+    batches.  ``resident``: copy every block once into one device buffer and
+    reuse it on later passes (no per-pass host transfers)."""
 
     def __init__(self, dev, x_host, p0, p1, BLOCK_N, K, D, dtype, resident: bool = False):
         self.dev = dev
         self.x_host = x_host
+        self.B = B = x_host.shape[0]
         self.p0, self.p1 = p0, p1
         self.BLOCK_N = BLOCK_N
         self.blocks = [(n0, min(n0 + BLOCK_N, p1)) for n0 in range(p0, p1, BLOCK_N)]
@@ -92,28 +97,31 @@ class _DeviceLane:
             nb = min(BLOCK_N, p1 - p0)
             if resident:
                 # one buffer for the whole slice; block i is rows n0-p0 .. n1-p0
-                self.xres = _ops.empty_rows(1, p1 - p0, D, dtype, dev)
+                self.xres = _ops.empty_rows(B, p1 - p0, D, dtype, dev)
                 self.res_loaded = [torch.cuda.Event() for _ in self.blocks]
                 self.res_issued = False
-            self.xbuf = [_ops.empty_rows(1, nb, D, dtype, dev) for _ in range(1 if resident else 2)]
+            self.xbuf = [_ops.empty_rows(B, nb, D, dtype, dev) for _ in range(1 if resident else 2)]
             self.stage = None
-            if x_host.dtype != dtype or not (x_host.is_contiguous() and self.xbuf[0].is_contiguous()):
-                self.stage = [torch.empty((nb, D), dtype=x_host.dtype, device=dev) for _ in range(2)]
+            if x_host.dtype != dtype or not (x_host[0].is_contiguous() and
+                                             self.xbuf[0].is_contiguous()):
+                # host rows land here, then one device kernel converts / pads them
+                self.stage = [torch.empty((B, nb, D), dtype=x_host.dtype, device=dev)
+                              for _ in range(2)]
             self.loaded = [torch.cuda.Event() for _ in range(2)]
             self.free = [torch.cuda.Event() for _ in range(2)]
-            self.labels = torch.empty((1, p1 - p0), dtype=torch.int32, device=dev)
+            self.labels = torch.empty((B, p1 - p0), dtype=torch.int32, device=dev)
             self.xsq = [None] * len(self.blocks)
-            self.c_cur = _ops.empty_rows(1, K, D, dtype, dev)
-            self.c_nxt = _ops.empty_rows(1, K, D, dtype, dev)
-            self.csq = torch.empty((1, K), dtype=torch.float32, device=dev)
-            self.sums = torch.empty((1, K, D), dtype=torch.float32, device=dev)
-            self.cnt = torch.empty((1, K), dtype=torch.int32, device=dev)
-            self.hist = torch.empty((1, K), dtype=torch.int32, device=dev)
+            self.c_cur = _ops.empty_rows(B, K, D, dtype, dev)
+            self.c_nxt = _ops.empty_rows(B, K, D, dtype, dev)
+            self.csq = torch.empty((B, K), dtype=torch.float32, device=dev)
+            self.sums = torch.empty((B, K, D), dtype=torch.float32, device=dev)
+            self.cnt = torch.empty((B, K), dtype=torch.int32, device=dev)
             self.stat = torch.zeros(4, dtype=torch.int32, device=dev)
+            self.stat_host = torch.empty(4, dtype=torch.int32, pin_memory=True)
             self.csq_valid = False
             lib = nat.load()
             self.ws = torch.empty(
-                lib.fk_assign_accumulate_workspace_size(1, nb, K, D, nat.dtype_code(dtype)),
+                lib.fk_assign_accumulate_workspace_size(B, nb, K, D, nat.dtype_code(dtype)),
                 dtype=torch.uint8, device=dev)
         # Copies form one sequence over passes: element s streams block s % nb
         # into buffer slot s % 2, so consecutive copies always alternate slots.
@@ -122,20 +130,28 @@ class _DeviceLane:
         self._pass = 0
 
     # ---------------------------------------------------------------- loads
+    def _copy_block(self, dst, stage, n0: int, n1: int) -> None:
+        """H2D copy of rows n0:n1 of every batch into dst (B, n1-n0, D) on
+        the current stream: one copy per batch (each a contiguous host range),
+        through `stage` when the rows need a dtype conversion or padding."""
+        nb = n1 - n0
+        for b in range(self.B):
+            src = self.x_host[b, n0:n1]
+            if stage is None:
+                dst[b].copy_(src, non_blocking=True)
+            else:
+                stage[b, :nb].copy_(src, non_blocking=True)
+        if stage is not None:
+            dst.copy_(stage[:, :nb])
+
     def _issue_load(self, blk: int, slot: int) -> None:
         n0, n1 = self.blocks[blk]
         nb = n1 - n0
         cs = self.copy_stream
         with torch.cuda.device(self.dev), torch.cuda.stream(cs):
             cs.wait_event(self.free[slot])
-            dst = self.xbuf[slot][0, :nb]
-            src = self.x_host[n0:n1]
-            if self.stage is None:
-                dst.copy_(src, non_blocking=True)
-            else:
-                st = self.stage[slot][:nb]
-                st.copy_(src, non_blocking=True)
-                dst.copy_(st)
+            self._copy_block(self.xbuf[slot][:, :nb],
+                             None if self.stage is None else self.stage[slot], n0, n1)
             self.loaded[slot].record(cs)
 
     def _prefetch_one(self) -> None:
@@ -161,15 +177,8 @@ class _DeviceLane:
         cs = self.copy_stream
         with torch.cuda.device(self.dev), torch.cuda.stream(cs):
             for i, (n0, n1) in enumerate(self.blocks):
-                nb = n1 - n0
-                dst = self.xres[0, n0 - self.p0:n1 - self.p0]
-                src = self.x_host[n0:n1]
-                if self.stage is None:
-                    dst.copy_(src, non_blocking=True)
-                else:
-                    st = self.stage[0][:nb]
-                    st.copy_(src, non_blocking=True)
-                    dst.copy_(st)
+                self._copy_block(self.xres[:, n0 - self.p0:n1 - self.p0],
+                                 None if self.stage is None else self.stage[0], n0, n1)
                 self.res_loaded[i].record(cs)
 
     # -------------------------------------------------------------- compute
@@ -178,7 +187,7 @@ class _DeviceLane:
         the first copies of the next pass are queued as buffers free up."""
         lib = nat.load()
         ks = self.compute_stream
-        K, D = self.K, self.D
+        B, K, D = self.B, self.K, self.D
         with torch.cuda.device(self.dev), torch.cuda.stream(ks):
             if not assign_only:
                 self.sums.zero_()
@@ -208,7 +217,7 @@ class _DeviceLane:
                 out = self.labels[:, lo:hi]
                 c_sq = self.csq if self.csq_valid else None
                 args = (nat.ptr(xb), nat.ptr(self.c_cur), nat.ptr(xsq), nat.ptr(c_sq), nat.ptr(out))
-                tail = (nat.dtype_code(xsq.dtype), nat.FK_F32, 1, nb, K, D, nat.strides(xb, 3),
+                tail = (nat.dtype_code(xsq.dtype), nat.FK_F32, B, nb, K, D, nat.strides(xb, 3),
                         nat.strides(self.c_cur, 3), nat.strides(xsq, 2), nat.strides(self.csq, 2),
                         nat.strides(out, 2), nat.ptr(self.ws), self.ws.numel(), status, s)
                 if assign_only:
@@ -228,7 +237,7 @@ class _DeviceLane:
         with torch.cuda.device(self.dev), torch.cuda.stream(self.compute_stream):
             nat.check(lib.fk_centroid_finalize(
                 nat.ptr(self.sums), nat.ptr(self.cnt), nat.ptr(self.c_cur), nat.ptr(self.c_nxt),
-                nat.dtype_code(self.dtype), 1, self.K, self.D, nat.strides(self.c_cur, 3),
+                nat.dtype_code(self.dtype), self.B, self.K, self.D, nat.strides(self.c_cur, 3),
                 nat.strides(self.c_nxt, 3), nat.ptr(self.csq), nat.ptr(self.stat[0:1]), 0,
                 nat.stream_handle(self.dev)), "fk_centroid_finalize")
             self.csq_valid = True
@@ -238,11 +247,24 @@ class _DeviceLane:
 
     def read_stat(self):
         """(shift, device status) after the work queued on the compute stream."""
-        host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+        host = self.stat_host
         with torch.cuda.device(self.dev), torch.cuda.stream(self.compute_stream):
             host.copy_(self.stat, non_blocking=True)
         self.compute_stream.synchronize()
         return host[0:1].view(torch.float32).item(), int(host[1].item())
+
+    def set_centroids(self, c0: torch.Tensor) -> None:
+        """Copy c0 (B, K, D), host or any device, into c_cur on the compute
+        stream, after whatever the caller's current streams have queued that
+        produces c0 (an init broadcast, a caller's kernel)."""
+        ks = self.compute_stream
+        with torch.cuda.device(self.dev):
+            ks.wait_stream(torch.cuda.current_stream(self.dev))
+            if c0.is_cuda and c0.device != self.dev:
+                ks.wait_stream(torch.cuda.current_stream(c0.device))
+            with torch.cuda.stream(ks):
+                self.c_cur.copy_(c0.to(self.dev, dtype=self.dtype, non_blocking=True))
+                self.stat.zero_()
 
 
 def reduce_partials(sums: torch.Tensor, counts: torch.Tensor, process_group) -> None:
@@ -284,6 +306,23 @@ def _check_status(code: int) -> None:
         raise RuntimeError(f"flash_kmeans device error {code}: {nat.device_status_message(code)}")
 
 
+def _as_host_batched(x: torch.Tensor):
+    """(N, D) -> (1, N, D) view, batched=False; (B, N, D) -> itself, batched=True."""
+    if x.dim() == 2:
+        return x.unsqueeze(0), False
+    if x.dim() == 3:
+        return x, True
+    raise ValueError("x must be (N, D) or (B, N, D)")
+
+
+def _gather_labels(lanes, B: int, N: int) -> torch.Tensor:
+    """Labels of all lanes into one pinned host tensor (B, N)."""
+    labels = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
+    for ln in lanes:
+        labels[:, ln.p0:ln.p1].copy_(ln.labels)
+    return labels
+
+
 def kmeans_largeN(
     x: torch.Tensor,
     n_clusters: int,
@@ -308,9 +347,13 @@ def kmeans_largeN(
     (extension): None keeps a device's slice of x in HBM after the first pass
     when it takes at most half of the free device memory and ``max_iters`` >
     1; False streams every pass like the reference; True keeps it resident
-    regardless (the allocation must succeed).
+    regardless (the allocation must succeed).  Batched x (B, N, D)
+    (extension; the reference supports (N, D) only) clusters the B problems
+    independently with the same pipeline; ``init_centroids`` is then
+    (B, K, D).
 
-    Returns (cluster_ids int32 (N,), centroids (K, D)).
+    Returns (cluster_ids int32 (N,), centroids (K, D)), or (B, N) and
+    (B, K, D) for batched x.
     """
     if not torch.cuda.is_available():
         raise RuntimeError("kmeans_largeN needs CUDA (this build has no CPU fallback)")
@@ -332,33 +375,38 @@ def kmeans_largeN(
             stacklevel=2,
         )
 
-    N, D = x.shape
+    xb, batched = _as_host_batched(x)
+    B, N, D = xb.shape
     K = int(n_clusters)
     blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
     active = [g for g in range(G) if blocks_per_gpu[g] > 0]
+
     def keep(g):
         if resident is not None:
             return bool(resident)
-        return max_iters > 1 and _fits_resident(devices[g], point_end[g] - point_start[g], D, dtype)
+        return max_iters > 1 and _fits_resident(devices[g], B * (point_end[g] - point_start[g]),
+                                                D, dtype)
 
-    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype,
+    lanes = [_DeviceLane(devices[g], xb, point_start[g], point_end[g], BLOCK_N, K, D, dtype,
                          resident=keep(g))
              for g in active]
     primary = lanes[0]
 
     # ---- initial centroids (replicated)
     if init_centroids is not None:
-        c0 = init_centroids.reshape(K, D)
-    elif distributed:
-        # x is this process's shard: sample on every rank, keep rank 0's
-        c0 = x[torch.randint(0, N, (K,), device="cpu", dtype=torch.int32)]
-        c0 = broadcast_centroids(c0.to(primary.dev, dtype=dtype).contiguous(), process_group)
+        c0 = init_centroids.reshape(B, K, D)
     else:
-        c0 = x[torch.randint(0, N, (K,), device="cpu", dtype=torch.int32)]
+        # random points, sampled on the host like the reference (kmeans_large.py:106-108)
+        if batched:
+            idx = torch.randint(0, N, (B, K), device="cpu")
+            c0 = torch.gather(xb, 1, idx[..., None].expand(-1, -1, D))
+        else:
+            c0 = x[torch.randint(0, N, (K,), device="cpu", dtype=torch.int32)].unsqueeze(0)
+        if distributed:
+            # x is this process's shard: every rank sampled, rank 0's sample wins
+            c0 = broadcast_centroids(c0.to(primary.dev, dtype=dtype).contiguous(), process_group)
     for ln in lanes:
-        with torch.cuda.device(ln.dev), torch.cuda.stream(ln.compute_stream):
-            ln.c_cur[0].copy_(c0.to(ln.dev, dtype=dtype, non_blocking=True))
-            ln.stat.zero_()
+        ln.set_centroids(c0)
 
     need_sync = tol > 0 or verbose
     tol_r = float(torch.tensor(float(tol), dtype=dtype))
@@ -391,14 +439,16 @@ def kmeans_largeN(
         _, code = ln.read_stat()
         _check_status(code)
 
-    centroids = primary.c_cur[0]
+    centroids = primary.c_cur
     centroids = centroids if centroids.is_contiguous() else centroids.contiguous()
     if G == 1 or distributed:
-        return primary.labels[0], centroids
-    labels = torch.empty((N,), dtype=torch.int32, pin_memory=True)
-    for ln in lanes:
-        labels[ln.p0:ln.p1].copy_(ln.labels[0])
-    return labels, centroids.cpu()
+        labels = primary.labels
+    else:
+        labels = _gather_labels(lanes, B, N)
+        centroids = centroids.cpu()
+    if not batched:
+        return labels[0], centroids[0]
+    return labels, centroids
 
 
 def kmeans_largeN_assign(
@@ -409,23 +459,23 @@ def kmeans_largeN_assign(
     dtype: Optional[torch.dtype] = None,
 ) -> torch.Tensor:
     """Labels for x (N, D) in host memory against centroids (K, D)
-    (kmeans_large.py:288-421).  One device -> labels on it; several -> pinned host."""
+    (kmeans_large.py:288-421).  One device -> labels on it; several -> pinned
+    host.  Batched x (B, N, D) with centroids (B, K, D) gives (B, N)."""
     if not torch.cuda.is_available():
         raise RuntimeError("kmeans_largeN_assign needs CUDA (this build has no CPU fallback)")
     devices = _resolve_devices(device)
     G = len(devices)
     dtype = dtype or x.dtype
-    N, D = x.shape
-    assert centroids.shape[1] == D, "centroids and x must have the same feature dimension"
-    K = centroids.shape[0]
+    xb, batched = _as_host_batched(x)
+    B, N, D = xb.shape
+    assert centroids.shape[-1] == D, "centroids and x must have the same feature dimension"
+    K = centroids.shape[-2]
     blocks_per_gpu, point_start, point_end = partition_blocks(N, BLOCK_N, G)
     active = [g for g in range(G) if blocks_per_gpu[g] > 0]
-    lanes = [_DeviceLane(devices[g], x, point_start[g], point_end[g], BLOCK_N, K, D, dtype)
+    lanes = [_DeviceLane(devices[g], xb, point_start[g], point_end[g], BLOCK_N, K, D, dtype)
              for g in active]
     for ln in lanes:
-        with torch.cuda.device(ln.dev), torch.cuda.stream(ln.compute_stream):
-            ln.c_cur[0].copy_(centroids.to(ln.dev, dtype=dtype, non_blocking=True))
-            ln.stat.zero_()
+        ln.set_centroids(centroids.reshape(B, K, D))
     for ln in lanes:
         ln.run_pass(assign_only=True)
     for ln in lanes:
@@ -433,9 +483,5 @@ def kmeans_largeN_assign(
             ln.compute_stream.synchronize()
         _, code = ln.read_stat()
         _check_status(code)
-    if G == 1:
-        return lanes[0].labels[0]
-    labels = torch.empty((N,), dtype=torch.int32, pin_memory=True)
-    for ln in lanes:
-        labels[ln.p0:ln.p1].copy_(ln.labels[0])
-    return labels
+    labels = lanes[0].labels if G == 1 else _gather_labels(lanes, B, N)
+    return labels if batched else labels[0]
