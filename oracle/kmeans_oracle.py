@@ -89,10 +89,12 @@ def assign(x, centroids, x_sq, dtype: str, xsq_dtype: str | None = None,
     each (N-chunk, K-chunk) the distance is
     ``x_sq[:, :, None] - 2 * bmm(x, c^T) + cent_sq[:, None, :]``
     (torch_fallback.py:41-45): the bmm result is rounded to ``dtype`` (float32
-    accumulation, one rounding), ``2 *`` is exact, the subtraction and the
-    addition each round to the promoted dtype.  There is no clamp.  The
-    distances land in a float32 buffer (torch_fallback.py:33) and ``argmin``
-    takes the first minimum (torch_fallback.py:50).  Returns int32 (B, N).
+    accumulation, one rounding), ``2 *`` is a separate op in that dtype (exact
+    unless it overflows to inf, e.g. |x.c| > 32752 in float16), the
+    subtraction and the addition each round to the promoted dtype.  There is
+    no clamp.  The distances land in a float32 buffer (torch_fallback.py:33)
+    and ``argmin`` takes the first minimum, or the first NaN if there is one
+    (torch_fallback.py:50; numpy's argmin does the same).  Returns int32 (B, N).
     """
     x = np.asarray(x, dtype=np.float32)
     c = np.asarray(centroids, dtype=np.float32)
@@ -112,8 +114,10 @@ def assign(x, centroids, x_sq, dtype: str, xsq_dtype: str | None = None,
             k1 = min(k0 + chunk_size_K, K)
             cross = np.matmul(x[:, n0:n1, :], np.swapaxes(c[:, k0:k1, :], 1, 2))
             cross = round_to(cross, dtype)
-            t = round_to(xs[:, n0:n1, None] - 2.0 * cross, t_dtype)
-            dists[:, :, k0:k1] = round_to(t + cent_sq[:, None, k0:k1], t_dtype)
+            with np.errstate(over="ignore", invalid="ignore"):
+                two = round_to(2.0 * cross, dtype)
+                t = round_to(xs[:, n0:n1, None] - two, t_dtype)
+                dists[:, :, k0:k1] = round_to(t + cent_sq[:, None, k0:k1], t_dtype)
         out[:, n0:n1] = np.argmin(dists, axis=-1)
     return out
 

@@ -32,6 +32,13 @@ ASSIGN_CASES = [
     dict(name="assign_f16_8193x1031", dtype="float16", B=1, N=8193, K=1031, D=128, seed=17),
     dict(name="assign_f32_8193x1031_d96", dtype="float32", B=1, N=8193, K=1031, D=96, seed=18),
     dict(name="assign_f32_d513", dtype="float32", B=1, N=600, K=70, D=513, seed=19),
+    # BASELINE config 4's feature size (split-D, 3xTF32): D=2048, float32
+    dict(name="assign_f32_d2048", dtype="float32", B=1, N=2048, K=256, D=2048, seed=20),
+    # float16 overflow: rows whose x_sq is inf, centroids whose c_sq is inf and
+    # cross products whose doubling leaves the float16 range, so distances
+    # reach inf and NaN (argmin then takes the first NaN, else the first minimum)
+    dict(name="assign_f16_overflow", dtype="float16", B=1, N=600, K=64, D=64, seed=25,
+         overflow=True),
 ]
 
 UPDATE_CASES = [
@@ -63,6 +70,16 @@ def assign_inputs(spec):
         c = np.concatenate([base, base], axis=1)
     else:
         c = ko.round_to(rng.standard_normal((B, K, D), dtype=np.float32), dt)
+    if spec.get("overflow"):
+        # rows N/3.. scaled by 30 (x_sq finite, some cross products overflow
+        # when doubled), rows 2N/3.. by 100 (x_sq = inf); a quarter of the
+        # centroids scaled by 100 (c_sq = inf), at random positions
+        scale = np.ones((B, N, 1), np.float32)
+        scale[:, N // 3:2 * N // 3] = 30.0
+        scale[:, 2 * N // 3:] = 100.0
+        x = ko.round_to(x * scale, dt)
+        big = rng.choice(K, size=K // 4, replace=False)
+        c[:, big] = ko.round_to(c[:, big] * np.float32(100.0), dt)
     if spec.get("xsq_f32"):
         xsq = np.square(x).sum(-1, dtype=np.float32)
         xsq_dtype = "float32"
@@ -98,7 +115,14 @@ def lloyd_inputs(spec):
 
 
 def checksum(*arrays) -> float:
-    return float(sum(np.asarray(a, dtype=np.float64).sum() for a in arrays))
+    """Sum of the finite values plus the number of non-finite ones (inputs of
+    the overflow cases hold inf)."""
+    total = 0.0
+    for a in arrays:
+        a = np.asarray(a, dtype=np.float64)
+        fin = np.isfinite(a)
+        total += float(a[fin].sum()) + float((~fin).sum())
+    return total
 
 
 def path(name: str) -> str:

@@ -23,7 +23,8 @@ the project's parity oracle) and records, for every spec in ``cases.py``:
   drive them (kmeans_triton_impl.py:118-188).
 
 An optional second argument names the groups to (re)write, comma separated:
-``assign,update,lloyd,normalize,sim`` (default: all).
+``assign,update,lloyd,normalize,sim`` (default: all); an optional third one
+names the cases to (re)write within those groups (default: all).
 
 Inputs are rebuilt from their seeds by ``cases.py``; fixtures store outputs and
 an input checksum.  Nothing at test time reads the reference checkout.
@@ -54,13 +55,13 @@ def _np(t):
 GROUPS = ("assign", "update", "lloyd", "normalize", "sim")
 
 
-def main(ref_root: str, groups=GROUPS) -> None:
+def main(ref_root: str, groups=GROUPS, only=None) -> None:
     sys.path.insert(0, ref_root)
     from flash_kmeans import torch_fallback as tf  # the reference's oracle
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if "assign" in groups:
-        _assign(tf)
+        _assign(tf, only)
     if "update" in groups:
         _update(tf)
     if "lloyd" in groups:
@@ -71,8 +72,10 @@ def main(ref_root: str, groups=GROUPS) -> None:
         _similarity(tf)
 
 
-def _assign(tf):
+def _assign(tf, only=None):
     for spec in cases.ASSIGN_CASES:
+        if only and spec["name"] not in only:
+            continue
         x, c, xsq, xsq_dtype = cases.assign_inputs(spec)
         dt = spec["dtype"]
         ids = tf.euclid_assign_torch_native_chunked(_t(x, dt), _t(c, dt), _t(xsq, xsq_dtype))
@@ -182,6 +185,7 @@ def _similarity(tf):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) not in (2, 3):
-        sys.exit("usage: make_golden.py /path/to/flash-kmeans-checkout [group,...]")
-    main(sys.argv[1], tuple(sys.argv[2].split(",")) if len(sys.argv) == 3 else GROUPS)
+    if len(sys.argv) not in (2, 3, 4):
+        sys.exit("usage: make_golden.py /path/to/flash-kmeans-checkout [group,...] [case,...]")
+    main(sys.argv[1], tuple(sys.argv[2].split(",")) if len(sys.argv) >= 3 else GROUPS,
+         set(sys.argv[3].split(",")) if len(sys.argv) == 4 else None)
