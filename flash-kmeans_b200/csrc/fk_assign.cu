@@ -14,18 +14,22 @@
 // optionally, +1 on that label's count, or with fused accumulation the point's
 // row added to its cluster's float32 sum).
 //
-// Roles (warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
-// 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4).. and column half
-// (w-2)/4 of each 256-column tile), then 4 more warps: f32 split converters
+// Roles (warps): 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2-3 idle
+// (the three form warpgroup 0, which gives most of its registers away),
+// 4..11 = epilogue (warp w reads TMEM lanes 32*(w%4).. and column half
+// (w-4)/4 of each 256-column tile), then 4 more warps: f32 split converters
 // (3xTF32 mode) or sum warps (fused accumulation).
 //
 // Modes:
-//   0  16-bit x with x_sq in the same dtype: dist = r(r(x_sq - 2 r(x.c)) + c_sq),
+//   0  16-bit x with x_sq in the same dtype: dist = r(r(x_sq - r(2 r(x.c))) + c_sq),
 //      r = round to that dtype, evaluated two columns at a time on packed
 //      half2 / bfloat162 registers.  This is the reference torch path's op
-//      chain (torch_fallback.py:41-45) with no clamp.
-//   1  16-bit x, float32 x_sq: cross rounded to the 16-bit dtype (the bmm output
-//      dtype), then the float32 chain (type promotion of torch_fallback.py:41-45).
+//      chain (torch_fallback.py:41-45) with no clamp, overflow of 2 r(x.c)
+//      to inf included: the centroid operand is -2c (staged by the host), so
+//      the accumulator holds -2 x.c and one conversion rounds it.
+//   1  16-bit x, float32 x_sq: the same -2 x.c rounded to the 16-bit dtype (the
+//      bmm output dtype), then the float32 chain (type promotion of
+//      torch_fallback.py:41-45).
 //   2  float32 x: cross = 3xTF32 (hi*hi + hi*lo + lo*hi, hi = tf32-rounded
 //      value, lo = exact remainder, split in shared memory by the 4 extra warps),
 //      float32 chain.
@@ -38,6 +42,7 @@
 // Split-D: when the x tile (128 points x D) does not fit twice in shared
 // memory (more than two 128-byte column chunks) the x chunk travels with each
 // centroid chunk instead of staying resident.
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -51,9 +56,18 @@ constexpr int kCent = 256;            // centroids per tile (MMA N); 128 for K <
 constexpr int kTmemCols = 512;        // accumulators: kTmemCols / tile width of them
 constexpr int kChunkB = 128;          // bytes per row chunk = one 128B swizzle span
 constexpr int kXChunk = kRows * kChunkB;   // 16 KB
-constexpr int kEpiWarp0 = 2;           // epilogue warps start here (EPI of them)
+// Warpgroup 0 = TMA producer (warp 0), MMA issuer (warp 1), two idle warps;
+// warpgroups 1-2 = epilogue; warpgroup 3 (when present) = split converters or
+// sum warps.  Roles follow warpgroups so each can get its own register budget.
+constexpr int kEpiWarp0 = 4;           // epilogue warps start here (EPI of them)
 constexpr int kConvWarps = 4;          // fp32 split warps / sum warps after the epilogue
 constexpr int kResidentChunks = 2;    // resident x: at most 2 chunks (D <= 128 for 16-bit)
+
+// Bytes of the workspace's c_sq part: B x (K padded to 256-column tiles) x 4.
+inline size_t assign_csq_bytes(int64_t B, int64_t K) {
+  const int64_t kpad = (K + kCent - 1) / kCent * kCent;
+  return align_up(static_cast<size_t>(B * kpad * 4), 256);
+}
 
 // Modes 2 and 4 split float32 operands into tf32 hi/lo parts (converter warps).
 constexpr bool split_mode(int mode) { return mode == 2 || mode == 4; }
@@ -95,8 +109,20 @@ struct Layout {
   static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
-  static constexpr int threads =
-      (kEpiWarp0 + EPI + ((split_mode(MODE) || FUSE) ? kConvWarps : 0)) * 32;
+  static constexpr bool kExtra = split_mode(MODE) || FUSE;  // warpgroup 3
+  static constexpr int threads = (kEpiWarp0 + EPI + (kExtra ? kConvWarps : 0)) * 32;
+  // Register budgets (setmaxnreg).  kLaunchRegs is what ptxas gives a thread
+  // under __launch_bounds__(threads, 1); the host checks the kernel's actual
+  // count before launching.  Control warps shrink to kCtlRegs, the extra
+  // warpgroup to kExtraRegs, and the epilogue takes the rest.
+  static constexpr int kLaunchRegs = threads == 384 ? 168 : 128;
+  static constexpr int kCtlRegs = 72;
+  static constexpr int kExtraRegs = FUSE ? 96 : 72;
+  static constexpr int kEpiRegs =
+      ((threads * kLaunchRegs - 128 * kCtlRegs - (kExtra ? 128 * kExtraRegs : 0)) / (EPI * 32)) & ~7;
+  static_assert(EPI == 8, "two epilogue warpgroups");
+  static_assert(threads == 384 || threads == 512, "three or four warpgroups");
+  static_assert(kEpiRegs <= 256 && kEpiRegs >= kLaunchRegs, "epilogue register budget");
 };
 
 struct AssignParams {
@@ -129,28 +155,61 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, uint6
 }
 
 // ---------------------------------------------------------------- epilogue math
-// Packed 16-bit helpers (mode 0).
+// Packed 16-bit helpers (mode 0).  In modes 0 and 1 the MMA's centroid
+// operand is -2c, so the float32 accumulator holds -2 x.c exactly and one
+// round-to-nearest conversion gives round(-2 * round(x.c)): the reference's
+// `2 * bmm(x, c^T)` in the 16-bit dtype, overflow to inf included (the two
+// differ only when x.c is a float16 subnormal, |x.c| < 2^-14).
 template <typename T>
 struct Pack2;
 
+#define FK_PACK2_OPS(SFX, INF2)                                                                  \
+  static constexpr uint32_t kInf2 = INF2;                                                        \
+  /* round(round(x_sq + round(acc)) + c_sq) for two columns, lo = even column */                 \
+  __device__ __forceinline__ static uint32_t dist(float a0, float a1, uint32_t xsq2,             \
+                                                  uint32_t csq2) {                               \
+    uint32_t r;                                                                                  \
+    asm("{\n\t.reg .b32 t;\n\t"                                                                  \
+        "cvt.rn." SFX ".f32 t, %2, %1;\n\t"                                                      \
+        "add.rn." SFX " t, %3, t;\n\t"                                                           \
+        "add.rn." SFX " %0, t, %4;\n\t}"                                                         \
+        : "=r"(r)                                                                                \
+        : "f"(a0), "f"(a1), "r"(xsq2), "r"(csq2));                                               \
+    return r;                                                                                    \
+  }                                                                                              \
+  /* minimum that propagates NaN (argmin takes the first NaN) */                                 \
+  __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {                      \
+    uint32_t r;                                                                                  \
+    asm("min.NaN." SFX " %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));                               \
+    return r;                                                                                    \
+  }                                                                                              \
+  /* on a strict improvement of the chunk minimum mm over best2 (or the first NaN),    */        \
+  /* store the chunk's 16 packed distances as four 16-byte units `STRIDE` bytes apart  */        \
+  /* at shared address `saddr`, and take mm and `tag` as the new best and saved chunk. */        \
+  template <int STRIDE>                                                                          \
+  __device__ __forceinline__ static void save_if_better(uint32_t& best2, int& chunk,             \
+                                                        uint32_t mm, int tag, uint32_t saddr,    \
+                                                        const uint32_t (&d)[16]) {               \
+    asm volatile(                                                                                \
+        "{\n\t.reg .pred p, q, n;\n\t"                                                           \
+        "setp.nan." SFX " n|q, %0, %0;\n\t"                                                      \
+        "setp.ltu.and." SFX " p|q, %2, %0, !n;\n\t"                                              \
+        "@p st.shared.v4.b32 [%4], {%6, %7, %8, %9};\n\t"                                        \
+        "@p st.shared.v4.b32 [%4+%5], {%10, %11, %12, %13};\n\t"                                 \
+        "@p st.shared.v4.b32 [%4+2*%5], {%14, %15, %16, %17};\n\t"                               \
+        "@p st.shared.v4.b32 [%4+3*%5], {%18, %19, %20, %21};\n\t"                               \
+        "selp.b32 %0, %2, %0, p;\n\t"                                                            \
+        "selp.b32 %1, %3, %1, p;\n\t}"                                                           \
+        : "+r"(best2), "+r"(chunk)                                                               \
+        : "r"(mm), "r"(tag), "r"(saddr), "n"(STRIDE), "r"(d[0]), "r"(d[1]), "r"(d[2]),           \
+          "r"(d[3]), "r"(d[4]), "r"(d[5]), "r"(d[6]), "r"(d[7]), "r"(d[8]), "r"(d[9]),           \
+          "r"(d[10]), "r"(d[11]), "r"(d[12]), "r"(d[13]), "r"(d[14]), "r"(d[15])                 \
+        : "memory");                                                                             \
+  }
+
 template <>
 struct Pack2<__half> {
-  using V = __half2;
-  static constexpr uint32_t kInf2 = 0x7C007C00u;
-  __device__ __forceinline__ static uint32_t dist(float c0, float c1, uint32_t xsq2, uint32_t csq2) {
-    const __half2 cr = __floats2half2_rn(c0, c1);  // .x = even column
-    const __half2 neg2 = __float2half2_rn(-2.0f);
-    const __half2 t = __hfma2(cr, neg2, *reinterpret_cast<const __half2*>(&xsq2));
-    const __half2 d = __hadd2(t, *reinterpret_cast<const __half2*>(&csq2));
-    return *reinterpret_cast<const uint32_t*>(&d);
-  }
-  __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
-    return __hlt2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
-  }
-  __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
-    const __half2 r = __hmin2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
-    return *reinterpret_cast<const uint32_t*>(&r);
-  }
+  FK_PACK2_OPS("f16x2", 0x7C007C00u)
   __device__ __forceinline__ static float lo(uint32_t v) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
   }
@@ -165,24 +224,7 @@ struct Pack2<__half> {
 
 template <>
 struct Pack2<__nv_bfloat16> {
-  using V = __nv_bfloat162;
-  static constexpr uint32_t kInf2 = 0x7F807F80u;
-  __device__ __forceinline__ static uint32_t dist(float c0, float c1, uint32_t xsq2, uint32_t csq2) {
-    const __nv_bfloat162 cr = __floats2bfloat162_rn(c0, c1);
-    const __nv_bfloat162 neg2 = __float2bfloat162_rn(-2.0f);
-    const __nv_bfloat162 t = __hfma2(cr, neg2, *reinterpret_cast<const __nv_bfloat162*>(&xsq2));
-    const __nv_bfloat162 d = __hadd2(t, *reinterpret_cast<const __nv_bfloat162*>(&csq2));
-    return *reinterpret_cast<const uint32_t*>(&d);
-  }
-  __device__ __forceinline__ static uint32_t lt_mask(uint32_t a, uint32_t b) {
-    return __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
-                       *reinterpret_cast<const __nv_bfloat162*>(&b));
-  }
-  __device__ __forceinline__ static uint32_t min2(uint32_t a, uint32_t b) {
-    const __nv_bfloat162 r = __hmin2(*reinterpret_cast<const __nv_bfloat162*>(&a),
-                                     *reinterpret_cast<const __nv_bfloat162*>(&b));
-    return *reinterpret_cast<const uint32_t*>(&r);
-  }
+  FK_PACK2_OPS("bf16x2", 0x7F807F80u)
   __device__ __forceinline__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
   __device__ __forceinline__ static float hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
   __device__ __forceinline__ static uint32_t splat(float v) {
@@ -190,11 +232,20 @@ struct Pack2<__nv_bfloat16> {
     return *reinterpret_cast<const uint32_t*>(&h);
   }
 };
+#undef FK_PACK2_OPS
 
 // Round a float to the 16-bit type and back (mode 1 cross rounding).
 template <typename T>
 __device__ __forceinline__ float round16(float v) {
   return Elem<T>::round(v);
+}
+
+// Candidate (vo, io) beats (val, idx) under argmin's rules: the first NaN
+// wins, otherwise the smaller value, then the lower index.
+__device__ __forceinline__ bool argmin_better(float vo, int io, float val, int idx) {
+  const bool nv = vo != vo, nc = val != val;
+  if (nv || nc) return nv && (!nc || io < idx);
+  return vo < val || (vo == val && io < idx);
 }
 
 // Running argmin over a thread's row for the float32-chain modes, split into
@@ -207,29 +258,30 @@ __device__ __forceinline__ float round16(float v) {
 // chunk where the best value changed.
 constexpr int kChains = 4;
 
-// Running argmin for mode 0 that spends about one ALU operation per column
-// pair: each 32-column chunk is reduced to its minimum with a tree of packed
-// min operations and compared once with the running best.  When a thread's
-// chunk minimum is strictly below its best, the thread stores the chunk's 16
-// packed distances in its own shared-memory slot (predicated stores on the
-// otherwise idle load/store pipe).  The saved chunk is then the first chunk
-// holding the final minimum (later chunks that only tie are not saved), so
-// the first column equal to the minimum inside it is the lowest-index
-// argmin.  result() finds that column once per tile.
+// Running argmin for mode 0 at about one ALU operation per column pair: each
+// 32-column chunk is reduced to its minimum with a tree of packed NaN-
+// propagating min operations and compared once with the running best.  When
+// the chunk minimum is strictly below the best (or is the row's first NaN),
+// the thread stores the chunk's 16 packed distances in its own shared-memory
+// slot with predicated stores (no branch).  The saved chunk is then the first
+// chunk holding the final minimum (later chunks that only tie are not
+// saved), so the first column equal to the minimum inside it (the first NaN
+// if the minimum is NaN) is argmin's lowest-index answer; result() finds it
+// once per point tile.
 template <typename T>
 struct ArgminSaved {
   uint32_t best2;  // running minimum, in both halves
   int chunk;       // col >> 5 of the saved chunk, -1 while nothing is saved
-  uint4* slot;     // this thread's four 16-byte units, `stride` units apart
-  int stride;
-  __device__ __forceinline__ void init(uint4* s, int st) {
+  uint32_t saddr;  // shared address of this thread's first 16-byte unit
+  __device__ __forceinline__ void init(uint32_t slot_addr) {
     best2 = Pack2<T>::kInf2;
     chunk = -1;
-    slot = s;
-    stride = st;
+    saddr = slot_addr;
   }
-  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint32_t* cw,
+  template <int STRIDE>
+  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint4 (&cq)[4],
                                           uint32_t xsq2, int col0) {
+    const uint32_t* cw = reinterpret_cast<const uint32_t*>(cq);
     uint32_t d[16];
 #pragma unroll
     for (int pp = 0; pp < 16; ++pp)
@@ -243,16 +295,11 @@ struct ArgminSaved {
     m[1] = Pack2<T>::min2(m[1], m[3]);
     m[0] = Pack2<T>::min2(m[0], m[1]);
     const uint32_t mm = Pack2<T>::min2(m[0], __byte_perm(m[0], 0, 0x1032));  // both halves
-    if (Pack2<T>::lt_mask(mm, best2) != 0u) {
-      best2 = mm;
-      chunk = col0 >> 5;
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        slot[u * stride] = make_uint4(d[4 * u], d[4 * u + 1], d[4 * u + 2], d[4 * u + 3]);
-    }
+    Pack2<T>::template save_if_better<STRIDE>(best2, chunk, mm, col0 >> 5, saddr, d);
   }
   // first_col: the lowest column this thread visits (the answer when every
   // distance it saw was +inf, matching argmin's first index)
+  template <int STRIDE>
   __device__ __forceinline__ void result(float& val, int& idx, int first_col) const {
     val = __int_as_float(0x7f800000);
     idx = first_col;
@@ -260,18 +307,25 @@ struct ArgminSaved {
     val = Pack2<T>::lo(best2);
     uint32_t w[16];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint4 q = slot[u * stride];
-      w[4 * u] = q.x;
-      w[4 * u + 1] = q.y;
-      w[4 * u + 2] = q.z;
-      w[4 * u + 3] = q.w;
-    }
+    for (int u = 0; u < 4; ++u)
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w[4 * u]), "=r"(w[4 * u + 1]), "=r"(w[4 * u + 2]), "=r"(w[4 * u + 3])
+                   : "r"(saddr + u * STRIDE)
+                   : "memory");
     int pos = 31;
+    if (val != val) {  // the first NaN of the saved chunk
 #pragma unroll
-    for (int pp = 15; pp >= 0; --pp) {
-      if (Pack2<T>::hi(w[pp]) == val) pos = 2 * pp + 1;
-      if (Pack2<T>::lo(w[pp]) == val) pos = 2 * pp;
+      for (int pp = 15; pp >= 0; --pp) {
+        const float h = Pack2<T>::hi(w[pp]), l = Pack2<T>::lo(w[pp]);
+        if (h != h) pos = 2 * pp + 1;
+        if (l != l) pos = 2 * pp;
+      }
+    } else {
+#pragma unroll
+      for (int pp = 15; pp >= 0; --pp) {
+        if (Pack2<T>::hi(w[pp]) == val) pos = 2 * pp + 1;
+        if (Pack2<T>::lo(w[pp]) == val) pos = 2 * pp;
+      }
     }
     idx = chunk * 32 + pos;
   }
@@ -297,9 +351,14 @@ struct ArgminF32 {  // modes 1 and 2: one column per register, float32 chain
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int c = j % kChains;
-      float cr = __uint_as_float(v[j]);
-      if constexpr (MODE == 1) cr = round16<T>(cr);
-      const float d = __fadd_rn(__fmaf_rn(-2.0f, cr, xsq), cs[j]);
+      // mode 1: the accumulator is -2 x.c (operand -2c) and round16 gives the
+      // reference's float16 `2 * bmm(...)`, then the float32 chain;
+      // mode 2: float32 cross products, x_sq - 2 * cross rounded once
+      float d;
+      if constexpr (MODE == 1)
+        d = __fadd_rn(__fadd_rn(xsq, round16<T>(__uint_as_float(v[j]))), cs[j]);
+      else
+        d = __fadd_rn(__fmaf_rn(-2.0f, __uint_as_float(v[j]), xsq), cs[j]);
       const bool lt = d < best[c];
       best[c] = fminf(best[c], d);
       loc[c] = lt ? j : loc[c];
@@ -471,9 +530,13 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Each role's branch first moves its warpgroup's register budget
+  // (setmaxnreg, inside the branch so the compiler knows each role's limit):
+  // the control warps and the extra warpgroup give registers to the epilogue.
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    setmaxnreg_dec<L::kCtlRegs>();
     if (lane == 0) {
       int stage = 0;
       uint32_t sph = 0;
@@ -547,6 +610,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
+    setmaxnreg_dec<L::kCtlRegs>();
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(Elem<T>::kMmaFmt, kRows, kCent);
       int stage = 0;
@@ -638,8 +702,12 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       mma_commit(final_bar);
       drain_wait(final_bar, 0, 1000000000ull);
     }
+  } else if (warp < kEpiWarp0) {
+    // idle warps of warpgroup 0: straight to the final barrier
+    setmaxnreg_dec<L::kCtlRegs>();
   } else if (warp < kEpiWarp0 + kEpiWarps) {
     // ------------------------------------------------------------- epilogue
+    setmaxnreg_inc<L::kEpiRegs>();
     const int ew = warp - kEpiWarp0;
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int h = ew >> 2;           // column group: kGCols columns of each tile
@@ -667,8 +735,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       using Argmin = typename std::conditional<
           MODE == 0, ArgminSaved<T>,
           typename std::conditional<(MODE >= 3), ArgmaxSaved, ArgminF32<T, MODE>>::type>::type;
+      constexpr int kSaveStride = L::save_stride * 16;  // bytes between a slot's 16-byte units
       Argmin am;
-      if constexpr (MODE == 0 || MODE >= 3)
+      if constexpr (MODE == 0)
+        am.init(smem_u32(smem + L::save_off) + static_cast<uint32_t>((ew * 32 + lane) * 16));
+      else if constexpr (MODE >= 3)
         am.init(reinterpret_cast<uint4*>(smem + L::save_off) + ew * 32 + lane, L::save_stride);
       else
         am.init();
@@ -677,99 +748,118 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       const uint8_t* csq_row =
           static_cast<const uint8_t*>(p.csq) +
           static_cast<size_t>(b) * p.kpad * (MODE == 0 ? 2 : 4);
-
-      // The warp's chunks of this point tile in (centroid tile, chunk) order.
-      // The TMEM load and the c_sq loads of chunk g+1 are in flight while
-      // chunk g is reduced (tcgen05.wait::ld waits for every outstanding
-      // load, so at most one is outstanding); a centroid tile's accumulator
-      // is released as soon as its last chunk is in registers.
-      // 16-byte c_sq words per chunk prefetched with the TMEM load (packed
-      // 16-bit mode without fused sums).  The float32-chain modes load theirs
-      // when reducing, and so does the fused kernel: its 14 warps leave 128
-      // registers per thread, where the two prefetch sets spilled (0.86 ->
-      // 0.79 ms at B=32, N=75600, K=1000, D=128 without them).
-      constexpr bool kCsqPrefetch = MODE == 0 && !FUSE;
-      constexpr int kCsqVec = kCsqPrefetch ? 4 : 1;
-      static_assert(kGChunks % 2 == 0, "chunks per group must be even");
-      const int nchunks = p.nkt * kGChunks;
-      uint32_t va[32], vb[32];
-      uint4 ca[kCsqVec], cb[kCsqVec];
-      // Start the loads of chunk g (waiting for its accumulator first).
-      auto issue = [&](int g, uint32_t(&v)[32], uint4(&cq)[kCsqVec]) -> bool {
-        const int ch = g % kGChunks;
-        if (ch == 0) {
-          // warp-uniform outcome: tcgen05.ld is .sync.aligned
-          const bool got = mbar_wait(&acc_full[ab], aph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-          if (!__all_sync(0xffffffffu, got)) return false;
-          tc_fence_after();
-        }
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(ab * kCent + h * kGCols + ch * 32),
-                  v);
-        if constexpr (kCsqPrefetch) {
-          const int col0 = (g / kGChunks) * kCent + h * kGCols + ch * 32;
-          const uint4* src = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
-#pragma unroll
-          for (int i = 0; i < kCsqVec; ++i) cq[i] = __ldg(src + i);
-        }
+      // Wait for accumulator `ab` (warp-uniform outcome: tcgen05.ld is .sync.aligned).
+      auto acc_wait = [&]() -> bool {
+        const bool got = mbar_wait(&acc_full[ab], aph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) return false;
+        tc_fence_after();
         return true;
       };
-      // Chunk g's registers have landed; hand back its accumulator if done.
-      auto landed = [&](int g, uint32_t(&v)[32]) {
-        tmem_ld_wait(v);
-        if (g % kGChunks == kGChunks - 1) {
-          tc_fence_before();
-          mbar_arrive(&acc_empty[ab]);
-          if (++ab == kAcc) { ab = 0; aph ^= 1; }
-        }
+      auto acc_release = [&]() {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[ab]);
+        if (++ab == kAcc) { ab = 0; aph ^= 1; }
       };
-      auto reduce = [&](int g, uint32_t(&v)[32], const uint4(&cq)[kCsqVec]) {
-        const int col0 = (g / kGChunks) * kCent + h * kGCols + (g % kGChunks) * 32;
-        if constexpr (kCsqPrefetch) {
-          am.chunk32(v, reinterpret_cast<const uint32_t*>(cq), xsq2, col0);
-        } else if constexpr (MODE == 0) {
-          const uint4* src = reinterpret_cast<const uint4*>(csq_row + col0 * 2);
-          uint4 c4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) c4[i] = __ldg(src + i);
-          am.chunk32(v, reinterpret_cast<const uint32_t*>(c4), xsq2, col0);
-        } else if constexpr (MODE >= 3) {
-          am.chunk32(v, col0, p.K);
-        } else {
-          const float4* src = reinterpret_cast<const float4*>(csq_row + col0 * 4);
-          float4 c4[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) c4[i] = __ldg(src + i);
-          am.chunk32(v, reinterpret_cast<const float*>(c4), xsq_f, col0);
-        }
-      };
-      if (!issue(0, va, ca)) {
-        ok = false;
-        break;
-      }
-      landed(0, va);
-#pragma unroll 1
-      for (int g = 0; g < nchunks; g += 2) {
-        if (!issue(g + 1, vb, cb)) {
-          ok = false;
-          break;
-        }
-        reduce(g, va, ca);
-        landed(g + 1, vb);
-        const bool more = g + 2 < nchunks;
-        if (more && !issue(g + 2, va, ca)) {
-          ok = false;
-          break;
-        }
-        reduce(g + 1, vb, cb);
-        if (more) landed(g + 2, va);
-      }
-      if (!ok) break;
 
-      // Per-thread winner: (value, lowest column on ties).
+      if constexpr (MODE == 0) {
+        // Per centroid tile the warp loads its whole column slice (kCh
+        // 32-column chunks, kCh*32 registers) with back-to-back TMEM loads and
+        // one wait, hands the accumulator back at once and reduces from
+        // registers, so the accumulator is held only for the loads.  The chunk
+        // loop is unrolled (TMEM addresses and c_sq offsets are constants);
+        // each chunk's c_sq words are fetched one chunk ahead.
+        constexpr int kCh = kGCols / 32;
+        const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(h * kGCols);
+        const uint4* cs0 = reinterpret_cast<const uint4*>(csq_row) + h * kGCols / 8;
+        uint32_t v[kCh][32];
+        uint4 cq[2][4];
+        for (int kt = 0; kt < p.nkt; ++kt) {
+          if (!acc_wait()) {
+            ok = false;
+            break;
+          }
+          const uint32_t tt = tq + static_cast<uint32_t>(ab * kCent);
+#pragma unroll
+          for (int c = 0; c < kCh; ++c) tmem_ld32(tt + c * 32, v[c]);
+          const uint4* ct = cs0 + kt * (kCent / 8);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) cq[0][i] = __ldg(ct + i);
+#pragma unroll
+          for (int c = 0; c < kCh; ++c) tmem_ld_wait(v[c]);  // the first waits for all
+          acc_release();
+          const int colt = kt * kCent + h * kGCols;
+#pragma unroll
+          for (int c = 0; c < kCh; ++c) {
+            if (c + 1 < kCh) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) cq[(c + 1) & 1][i] = __ldg(ct + (c + 1) * 4 + i);
+            }
+            am.template chunk32<kSaveStride>(v[c], cq[c & 1], xsq2, colt + c * 32);
+          }
+        }
+        if (!ok) break;
+      } else {
+        // Modes 1-4: the chunks in (centroid tile, chunk) order; the TMEM load
+        // of chunk g+1 is in flight while chunk g is reduced; a tile's
+        // accumulator is released once its last chunk is in registers.  The
+        // float32 chains load their c_sq words when reducing.
+        const int nchunks = p.nkt * kGChunks;
+        uint32_t va[32], vb[32];
+        auto issue = [&](int g, uint32_t(&v)[32]) -> bool {
+          const int ch = g % kGChunks;
+          if (ch == 0 && !acc_wait()) return false;
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                        static_cast<uint32_t>(ab * kCent + h * kGCols + ch * 32),
+                    v);
+          return true;
+        };
+        auto landed = [&](int g, uint32_t(&v)[32]) {
+          tmem_ld_wait(v);
+          if (g % kGChunks == kGChunks - 1) acc_release();
+        };
+        auto reduce = [&](int g, uint32_t(&v)[32]) {
+          const int col0 = (g / kGChunks) * kCent + h * kGCols + (g % kGChunks) * 32;
+          if constexpr (MODE >= 3) {
+            am.chunk32(v, col0, p.K);
+          } else {
+            const float4* src = reinterpret_cast<const float4*>(csq_row + col0 * 4);
+            float4 c4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c4[i] = __ldg(src + i);
+            am.chunk32(v, reinterpret_cast<const float*>(c4), xsq_f, col0);
+          }
+        };
+        if (!issue(0, va)) {
+          ok = false;
+          break;
+        }
+        landed(0, va);
+#pragma unroll 1
+        for (int g = 0; g < nchunks; g += 2) {
+          if (!issue(g + 1, vb)) {
+            ok = false;
+            break;
+          }
+          reduce(g, va);
+          landed(g + 1, vb);
+          const bool more = g + 2 < nchunks;
+          if (more && !issue(g + 2, va)) {
+            ok = false;
+            break;
+          }
+          reduce(g + 1, vb);
+          if (more) landed(g + 2, va);
+        }
+        if (!ok) break;
+      }
+
+      // Per-thread winner: (value, lowest column on ties; the first NaN wins).
       float val;
       int idx;
-      if constexpr (MODE == 0 || MODE >= 3)
+      if constexpr (MODE == 0)
+        am.template result<kSaveStride>(val, idx, h * kGCols);
+      else if constexpr (MODE >= 3)
         am.result(val, idx, h * kGCols);
       else
         am.result(val, idx);
@@ -797,7 +887,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           const uint2 o = mslots[(gg - 1) * kRows + row];
           const float vo = __uint_as_float(o.x);
           const int io = static_cast<int>(o.y);
-          if (vo < val || (vo == val && io < idx)) {
+          if (argmin_better(vo, io, val, idx)) {
             val = vo;
             idx = io;
           }
@@ -830,6 +920,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     // read the warp releases the label slot; once its rows are in registers
     // it releases the x buffer.  Runs concurrently with the next tile's
     // epilogue.
+    if constexpr (L::kExtraRegs < L::kLaunchRegs) setmaxnreg_dec<L::kExtraRegs>();
     if constexpr (FUSE && XRES && sizeof(T) == 2) {
     const int sw = warp - kConvWarp0;  // 0..3
     const int col = 4 * lane;
@@ -882,6 +973,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
   } else if (split_mode(MODE)) {
     // ------------------------------------- 3xTF32 split converters (modes 2, 4)
+    if constexpr (L::kExtraRegs < L::kLaunchRegs) setmaxnreg_dec<L::kExtraRegs>();
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
     int stage = 0;
     uint32_t sph = 0;
@@ -944,12 +1036,30 @@ static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const Ass
   if (RESC && p.nkt * p.nd > STAGES) return fail(FK_ERR_UNSUPPORTED, "resident centroids do not fit");
   auto kern = assign_kernel<T, MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
   const int dev = current_device();
-  static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "bad current device %d", dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
-    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_set[dev] = true;
+  // Once per device and instance (only a successful set-up is remembered):
+  // allow the dynamic shared memory, and check that the launch allocation
+  // covers the warpgroups' register budgets (setmaxnreg.inc would otherwise
+  // wait forever for registers that do not exist).
+  static std::atomic<bool> ready[64];
+  static std::mutex setup_mu;
+  if (!ready[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (!ready[dev].load(std::memory_order_relaxed)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+      if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+      const long budget = 128L * L::kCtlRegs + 32L * EPI * L::kEpiRegs +
+                          (L::kExtra ? 128L * L::kExtraRegs : 0L);
+      if (static_cast<long>(fa.numRegs) * L::threads < budget || fa.numRegs > L::kLaunchRegs)
+        return fail(FK_ERR_UNSUPPORTED,
+                    "assign_kernel register split: %d registers x %d threads at launch, budgets "
+                    "need %ld",
+                    fa.numRegs, L::threads, budget);
+      ready[dev].store(true, std::memory_order_release);
+    }
   }
   const int sms = sm_count_current();
   if (sms <= 0) return fail(FK_ERR_CUDA, "could not query SM count");
@@ -958,13 +1068,20 @@ static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const Ass
   return check_launch("assign_kernel");
 }
 
-// Padded per-centroid squared norms in the epilogue's distance dtype.
-// Modes 0/1 follow (c ** 2).sum(-1) in the 16-bit dtype (torch_fallback.py:23);
-// mode 2 in float32.  A caller-provided c_sq is converted instead.
+// Stages the centroid-side operands of a Euclidean assignment:
+// * csq_out (B, kpad): per-centroid squared norms in the epilogue's distance
+//   dtype, +inf past K.  Modes 0/1 follow (c ** 2).sum(-1) in the 16-bit dtype
+//   (torch_fallback.py:23), mode 2 float32; a caller-provided c_sq is
+//   converted instead.
+// * cneg (B, K, dp), modes 0/1 only: -2c in the 16-bit dtype, the MMA's
+//   centroid operand (exact; saturated to the largest finite value where 2|c|
+//   leaves the range).
+// One warp per padded centroid row.
 template <typename T, int MODE>
-__global__ void prep_csq_kernel(const T* __restrict__ c, int64_t scb, int64_t sck, int64_t scd,
-                                const void* csq_in, int csq_dtype, int64_t sqb, int64_t sqk,
-                                void* csq_out, int64_t kpad, int B, int K, int D) {
+__global__ void prep_centroids_kernel(const T* __restrict__ c, int64_t scb, int64_t sck,
+                                      int64_t scd, const void* csq_in, int csq_dtype, int64_t sqb,
+                                      int64_t sqk, void* csq_out, int64_t kpad, T* cneg,
+                                      int64_t dp, int B, int K, int D) {
   const int warps_per_block = blockDim.x >> 5;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -972,20 +1089,20 @@ __global__ void prep_csq_kernel(const T* __restrict__ c, int64_t scb, int64_t sc
   for (int64_t r = gw; r < total; r += static_cast<int64_t>(gridDim.x) * warps_per_block) {
     const int b = static_cast<int>(r / kpad);
     const int k = static_cast<int>(r % kpad);
-    float v;
-    if (k >= K) {
-      v = __int_as_float(0x7f800000);
-    } else if (csq_in) {
-      v = load_f(csq_in, b * sqb + k * sqk, csq_dtype);
-    } else {
+    float v = __int_as_float(0x7f800000);
+    if (k < K) {
       const T* row = c + b * scb + k * sck;
+      T* nrow = cneg ? cneg + (static_cast<int64_t>(b) * K + k) * dp : nullptr;
       float acc = 0.0f;
       for (int d = lane; d < D; d += 32) {
         const float e = Elem<T>::to_f(row[d * scd]);
         acc += (MODE == 2) ? e * e : Elem<T>::round(e * e);
+        if (nrow) nrow[d] = Elem<T>::from_f(fminf(fmaxf(-2.0f * e, -Elem<T>::kMaxFinite),
+                                                  Elem<T>::kMaxFinite));
       }
       acc = warp_sum(acc);
-      v = (MODE == 2) ? acc : Elem<T>::round(acc);
+      v = csq_in ? load_f(csq_in, b * sqb + k * sqk, csq_dtype)
+                 : ((MODE == 2) ? acc : Elem<T>::round(acc));
     }
     if (lane == 0) {
       if (MODE == 0)
@@ -1033,19 +1150,20 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   const int nkt = static_cast<int>((K + kc - 1) / kc);
   const int64_t kpad = static_cast<int64_t>(nkt) * kc;
 
-  // 1) padded c_sq in the distance dtype (the dot-product modes have none:
-  //    their epilogue masks the padding columns itself)
+  // 1) padded c_sq in the distance dtype and, for the 16-bit Euclidean modes,
+  //    the -2c operand (the dot-product modes stage nothing: their epilogue
+  //    masks the padding columns itself)
+  const int64_t dp = static_cast<int64_t>(align_up(static_cast<size_t>(D), 8));
+  T* cneg = nullptr;
+  if (!dot && is16)
+    cneg = reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + assign_csq_bytes(B, K));
   if (dot) {
     // nothing to stage
-  } else if (c_sq) {
+  } else if (c_sq && mode == 2) {
     const int64_t total = B * kpad;
     const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-    if (mode == 0)
-      copy_csq_kernel<T, 0><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
-                                                         (int)K, total);
-    else
-      copy_csq_kernel<T, 1><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
-                                                         (int)K, total);
+    copy_csq_kernel<T, 2><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
+                                                       (int)K, total);
     int st = check_launch("copy_csq_kernel");
     if (st != FK_OK) return st;
   } else {
@@ -1053,27 +1171,31 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
     const int64_t rows = B * kpad;
     const int blocks = static_cast<int>(rows / 8 + 1 < 4096 ? rows / 8 + 1 : 4096);
     const T* c = static_cast<const T*>(cent);
+    const int64_t sqb = c_sq ? cqs[0] : 0, sqk = c_sq ? cqs[1] : 0;
     if (mode == 0)
-      prep_csq_kernel<T, 0><<<blocks, threads, 0, stream>>>(
-          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
-          (int)B, (int)K, (int)D);
+      prep_centroids_kernel<T, 0><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, sqb, sqk, ws, kpad, cneg, dp, (int)B, (int)K,
+          (int)D);
     else if (mode == 1)
-      prep_csq_kernel<T, 1><<<blocks, threads, 0, stream>>>(
-          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
-          (int)B, (int)K, (int)D);
+      prep_centroids_kernel<T, 1><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, sqb, sqk, ws, kpad, cneg, dp, (int)B, (int)K,
+          (int)D);
     else
-      prep_csq_kernel<T, 2><<<blocks, threads, 0, stream>>>(
-          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, c_sq ? cqs[0] : 0, c_sq ? cqs[1] : 0, ws, kpad,
-          (int)B, (int)K, (int)D);
-    int st = check_launch("prep_csq_kernel");
+      prep_centroids_kernel<T, 2><<<blocks, threads, 0, stream>>>(
+          c, cs[0], cs[1], cs[2], c_sq, csq_dtype, sqb, sqk, ws, kpad, nullptr, dp, (int)B,
+          (int)K, (int)D);
+    int st = check_launch("prep_centroids_kernel");
     if (st != FK_OK) return st;
   }
 
-  // 2) tensor maps: x as (D, N, B), centroids as (D, K, B), 128-byte swizzle
+  // 2) tensor maps: x as (D, N, B), centroids (or -2c) as (D, K, B), 128-byte swizzle
   CUtensorMap tx, tc;
   int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows);
   if (st != FK_OK) return st;
-  st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc);
+  if (cneg)
+    st = encode_tmap_3d(&tc, cneg, Elem<T>::kDtype, D, K, B, dp * eb, K * dp * eb, dch, kc);
+  else
+    st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc);
   if (st != FK_OK) return st;
 
   AssignParams p;
@@ -1140,11 +1262,15 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
 
 using namespace fk;
 
-extern "C" size_t fk_assign_workspace_size(int64_t B, int64_t K, int dtype) {
-  (void)dtype;
-  if (B <= 0 || K <= 0) return 256;
-  const int64_t kpad = (K + kCent - 1) / kCent * kCent;
-  return align_up(static_cast<size_t>(B * kpad * 4), 256) + 256;
+// Workspace of fk_assign: c_sq padded to whole 256-column tiles (4 bytes per
+// entry covers every mode), then for 16-bit x the -2c operand (B, K, D
+// rounded up to 8 elements).
+extern "C" size_t fk_assign_workspace_size(int64_t B, int64_t K, int64_t D, int dtype) {
+  if (B <= 0 || K <= 0 || D <= 0) return 256;
+  size_t bytes = assign_csq_bytes(B, K);
+  if (dtype == FK_F16 || dtype == FK_BF16)
+    bytes += align_up(static_cast<size_t>(B * K) * align_up(static_cast<size_t>(D), 8) * 2, 256);
+  return bytes + 256;
 }
 
 // fk_assign and fk_assign_dot: validation, TMA-friendly strides, dispatch.
@@ -1187,7 +1313,7 @@ static int assign_entry(const char* fn, bool dot, const void* x, const void* cen
     return fail(FK_ERR_UNSUPPORTED, "%s: x rows not TMA-addressable (pack with fk_pack_rows)", fn);
   if (!fk_tma_compatible(centroids, dtype, D, c_strides3))
     return fail(FK_ERR_UNSUPPORTED, "%s: centroid rows not TMA-addressable", fn);
-  const size_t need = fk_assign_workspace_size(B, K, dtype);
+  const size_t need = fk_assign_workspace_size(B, K, D, dtype);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(FK_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-aligned", fn, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1260,7 +1386,7 @@ extern "C" int fk_assign_accumulate_method(int64_t K, int64_t D, int dtype) {
 
 extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                       int dtype) {
-  const size_t wa = fk_assign_workspace_size(B, K, dtype);
+  const size_t wa = fk_assign_workspace_size(B, K, D, dtype);
   if (assign_accumulate_priv(K, D) || assign_accumulate_fused(K, D, dtype)) return wa;
   return wa + align_up(static_cast<size_t>(B > 0 && K > 0 ? B * K : 1) * 4, 256) +
          fk_centroid_accumulate_workspace_size(B, N, K);
@@ -1296,7 +1422,7 @@ static int assign_accumulate_entry(const char* fn, bool dot, const void* x, cons
                        dev_status, s);
   }
   if (!assign_accumulate_fused(K, D, dtype)) {
-    const size_t wa = fk_assign_workspace_size(B, K, dtype);
+    const size_t wa = fk_assign_workspace_size(B, K, D, dtype);
     int32_t* hist = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + wa);
     void* wu = static_cast<uint8_t*>(workspace) + wa + align_up(static_cast<size_t>(B * K) * 4, 256);
     cudaError_t e = cudaMemsetAsync(hist, 0, static_cast<size_t>(B * K) * 4, s);
@@ -1373,17 +1499,20 @@ extern "C" int fk_assign_dot_accumulate(const void* x, const void* centroids, in
 // server's custom-op interface with no workspace hook, a framework whose
 // memory pool forbids side allocations, or a latency-bound loop where
 // cudaMalloc/cudaFree (which can synchronise the device) is not acceptable.
-// This entry point needs no caller workspace: its scratch (the padded
-// per-centroid squared norms, B * ceil(K/256)*256 * 4 bytes plus 256) lives
-// in the file-scope device array below, which every GPU that loads this
-// library holds until the process exits.
+// This entry point needs no caller workspace: its scratch (what
+// fk_assign_workspace_size reports: the padded per-centroid squared norms
+// and, for 16-bit x, the -2c operand) lives in the file-scope device array
+// below, which every GPU that loads this library holds until the process
+// exits.
 //
-// * Limit: kAssignStaticScratchBytes = 1 MiB, i.e. B * ceil(K/256)*256 <= 262080
-//   (for example B=32 with K <= 8192, or B=1 with K <= 262080); larger
-//   problems are rejected with FK_ERR_WORKSPACE before anything is launched.
+// * Limit: kAssignStaticScratchBytes = 16 MiB, i.e.
+//   fk_assign_workspace_size(B, K, D, dtype) <= 16 MiB (for example B=32,
+//   K=1000, D=128 float16 needs 8.3 MiB); larger problems are rejected with
+//   FK_ERR_WORKSPACE before anything is launched.
 // * The first call on a device looks up the array's device address for that
 //   device (cudaGetSymbolAddress, with that device current); make that first
-//   call before any stream capture.
+//   call before any stream capture.  A failed lookup is not remembered: the
+//   next call tries again.
 // * All calls on a device share the one array and it keeps the last call's
 //   contents; every call rewrites all the scratch it reads, so nothing needs
 //   clearing, but calls that overlap on the GPU (different streams, or
@@ -1392,28 +1521,31 @@ extern "C" int fk_assign_dot_accumulate(const void* x, const void* centroids, in
 // ---------------------------------------------------------------------------
 namespace fk {
 
-constexpr size_t kAssignStaticScratchBytes = size_t(1) << 20;
+constexpr size_t kAssignStaticScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) uint8_t g_assign_static_scratch[kAssignStaticScratchBytes];
 
-struct StaticScratchSlot {
-  std::once_flag once;
-  void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-static StaticScratchSlot g_static_scratch_slots[64];
+// Per-device address of the array; only a successful lookup is kept.
+static std::atomic<void*> g_static_scratch_ptr[64];
+static std::mutex g_static_scratch_mu;
 
 static int static_scratch_for_current_device(void** out) {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return fail(FK_ERR_CUDA, "fk_assign_static_scratch: bad current device");
-  StaticScratchSlot& slot = g_static_scratch_slots[dev];
-  std::call_once(slot.once, [&slot] {
-    // runs with `dev` current: the caller's current device is this slot's device
-    slot.err = cudaGetSymbolAddress(&slot.ptr, g_assign_static_scratch);
-  });
-  if (slot.err != cudaSuccess || slot.ptr == nullptr)
-    return fail(FK_ERR_CUDA, "fk_assign_static_scratch: cudaGetSymbolAddress failed on device %d: %s",
-                dev, cudaGetErrorString(slot.err));
-  *out = slot.ptr;
+  void* ptr = g_static_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    ptr = g_static_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (ptr == nullptr) {
+      // runs with `dev` current: the caller's current device is this slot's device
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_assign_static_scratch);
+      if (e != cudaSuccess || ptr == nullptr)
+        return fail(FK_ERR_CUDA,
+                    "fk_assign_static_scratch: cudaGetSymbolAddress failed on device %d: %s", dev,
+                    cudaGetErrorString(e));
+      g_static_scratch_ptr[dev].store(ptr, std::memory_order_release);
+    }
+  }
+  *out = ptr;
   return FK_OK;
 }
 
@@ -1431,12 +1563,12 @@ extern "C" int fk_assign_static_scratch(const void* x, const void* centroids, co
     return fail(FK_ERR_INVALID_ARG, "fk_assign_static_scratch: bad sizes B=%lld N=%lld K=%lld D=%lld",
                 (long long)B, (long long)N, (long long)K, (long long)D);
   if (B == 0 || N == 0) return FK_OK;
-  const size_t need = fk_assign_workspace_size(B, K, dtype);
+  const size_t need = fk_assign_workspace_size(B, K, D, dtype);
   if (need > kAssignStaticScratchBytes)
     return fail(FK_ERR_WORKSPACE,
-                "fk_assign_static_scratch: B=%lld, K=%lld needs %zu bytes of scratch; the static "
-                "scratch holds %zu (B * ceil(K/256)*256 <= 262080); use fk_assign with a workspace",
-                (long long)B, (long long)K, need, kAssignStaticScratchBytes);
+                "fk_assign_static_scratch: B=%lld, K=%lld, D=%lld needs %zu bytes of scratch; the "
+                "static scratch holds %zu; use fk_assign with a workspace",
+                (long long)B, (long long)K, (long long)D, need, kAssignStaticScratchBytes);
   void* scratch = nullptr;
   const int st = static_scratch_for_current_device(&scratch);
   if (st != FK_OK) return st;

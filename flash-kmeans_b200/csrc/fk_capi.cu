@@ -2,6 +2,7 @@
 // TMA tensor-map encoding.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -40,15 +41,16 @@ int current_device() {
 }
 
 int sm_count_current() {
-  static int cache[64] = {0};
+  // per-device cache; concurrent first calls store the same value
+  static std::atomic<int> cache[64];
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return -1;
-  if (cache[dev] == 0) {
-    int v = 0;
+  int v = cache[dev].load(std::memory_order_acquire);
+  if (v == 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
-    cache[dev] = v;
+    cache[dev].store(v, std::memory_order_release);
   }
-  return cache[dev];
+  return v;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;

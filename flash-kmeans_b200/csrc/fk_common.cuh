@@ -21,6 +21,7 @@ struct Elem<__half> {
   static constexpr int kBytes = 2;
   static constexpr uint32_t kMmaFmt = 0;  // kind::f16, A/B format f16
   static constexpr int kDtype = FK_F16;
+  static constexpr float kMaxFinite = 65504.0f;
   __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
   __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
   __device__ __forceinline__ static float round(float v) { return __half2float(__float2half_rn(v)); }
@@ -31,6 +32,7 @@ struct Elem<__nv_bfloat16> {
   static constexpr int kBytes = 2;
   static constexpr uint32_t kMmaFmt = 1;  // kind::f16, A/B format bf16
   static constexpr int kDtype = FK_BF16;
+  static constexpr float kMaxFinite = 3.38953139e38f;
   __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
   __device__ __forceinline__ static float round(float v) {
@@ -43,6 +45,7 @@ struct Elem<float> {
   static constexpr int kBytes = 4;
   static constexpr uint32_t kMmaFmt = 2;  // kind::tf32
   static constexpr int kDtype = FK_F32;
+  static constexpr float kMaxFinite = 3.40282347e38f;
   __device__ __forceinline__ static float to_f(float v) { return v; }
   __device__ __forceinline__ static float from_f(float v) { return v; }
   __device__ __forceinline__ static float round(float v) { return v; }

@@ -208,6 +208,21 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
       : "memory");
 }
 
+// Per-warpgroup register budget changes (all four warps of a warpgroup
+// execute the same one).  An increase waits until the registers given up
+// by decreases are free, so the host checks, before the launch, that the
+// block's launch allocation covers the sum of the budgets.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(N >= 24 && N <= 256 && N % 8 == 0, "setmaxnreg range");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(N >= 24 && N <= 256 && N % 8 == 0, "setmaxnreg range");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor for a K-major operand stored with the
 // 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes (SBO), atom

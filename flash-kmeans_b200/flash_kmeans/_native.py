@@ -45,7 +45,7 @@ SIGNATURES = {
     "fk_row_sqnorm": (_I, [_P, _I, _L, _L, _L, _PL, _P, _I, _PL, _P]),
     "fk_row_normalize": (_I, [_P, _I, _L, _L, _L, _PL, _P, _PL, _P]),
     "fk_pack_rows": (_I, [_P, _I, _L, _L, _L, _PL, _P, _L, _P]),
-    "fk_assign_workspace_size": (_S, [_L, _L, _I]),
+    "fk_assign_workspace_size": (_S, [_L, _L, _L, _I]),
     "fk_assign": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL, _PL, _PL,
                        _PL, _P, _S, _P, _P]),
     "fk_assign_dot": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _L, _PL, _PL, _PL, _P, _S, _P, _P]),
@@ -65,7 +65,7 @@ SIGNATURES = {
                                              _P]),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lib = None
 _lock = threading.Lock()

@@ -127,7 +127,7 @@ def assign(x, centroids, x_sq, out=None, c_sq=None, counts=None, status=None) ->
     if out is None:
         out = torch.empty((B, N), dtype=torch.int32, device=x.device)
     lib = nat.load()
-    ws_bytes = lib.fk_assign_workspace_size(B, K, nat.dtype_code(x.dtype))
+    ws_bytes = lib.fk_assign_workspace_size(B, K, D, nat.dtype_code(x.dtype))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
     if status is None:
         status = DeviceStatus.word(x.device)
@@ -146,6 +146,28 @@ def _assign_call(lib, x, centroids, x_sq, out, c_sq, counts, ws, ws_bytes, statu
         B, N, K, D, nat.strides(x, 3), nat.strides(centroids, 3), nat.strides(x_sq, 2),
         nat.strides(c_sq, 2) if c_sq is not None else None, nat.strides(out, 2),
         nat.ptr(ws), ws_bytes, nat.ptr(status), nat.stream_handle(x.device)), "fk_assign")
+
+
+def assign_accumulate(x, centroids, x_sq, out, counts, sums, c_sq=None, status=None) -> None:
+    """Launch fk_assign_accumulate: labels into `out`, their histogram added to
+    `counts` and the rows of x added to sums[label] (one Lloyd iteration's
+    assignment and accumulation)."""
+    B, N, D = x.shape
+    K = centroids.shape[1]
+    lib = nat.load()
+    ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(x.dtype))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    if status is None:
+        status = DeviceStatus.word(x.device)
+    with torch.cuda.device(x.device):
+        nat.check(lib.fk_assign_accumulate(
+            nat.ptr(x), nat.ptr(centroids), nat.ptr(x_sq), nat.ptr(c_sq), nat.ptr(out),
+            nat.ptr(counts), nat.ptr(sums), nat.dtype_code(x.dtype), nat.dtype_code(x_sq.dtype),
+            nat.dtype_code(c_sq.dtype) if c_sq is not None else 0, B, N, K, D,
+            nat.strides(x, 3), nat.strides(centroids, 3), nat.strides(x_sq, 2),
+            nat.strides(c_sq, 2) if c_sq is not None else None, nat.strides(out, 2),
+            nat.ptr(ws), ws_bytes, nat.ptr(status), nat.stream_handle(x.device)),
+            "fk_assign_accumulate")
 
 
 def accumulate(x, ids, sums, counts, hist=None, status=None) -> None:
@@ -184,7 +206,7 @@ def assign_dot(x, centroids, out=None, counts=None, status=None) -> torch.Tensor
     if out is None:
         out = torch.empty((B, N), dtype=torch.int32, device=x.device)
     lib = nat.load()
-    ws_bytes = lib.fk_assign_workspace_size(B, K, nat.dtype_code(x.dtype))
+    ws_bytes = lib.fk_assign_workspace_size(B, K, D, nat.dtype_code(x.dtype))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
     if status is None:
         status = DeviceStatus.word(x.device)

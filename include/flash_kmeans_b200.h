@@ -56,7 +56,7 @@
 extern "C" {
 #endif
 
-#define FK_ABI_VERSION 1
+#define FK_ABI_VERSION 2
 
 /* element types */
 enum fk_dtype { FK_F16 = 0, FK_BF16 = 1, FK_F32 = 2, FK_I32 = 3, FK_I64 = 4 };
@@ -114,11 +114,14 @@ int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
  *   out (B,N) int32.  counts (B,K) int32 optional: if given, out's histogram is
  *   ADDED to it (the update's histogram, fused).
  * Distance rounding follows the reference's torch path: with x_sq in x's
- * 16-bit dtype the chain is round(round(x_sq - 2*round(x.c)) + c_sq) in that
- * dtype; otherwise float32 (for float32 x the dot products are 3xTF32 on the
- * tensor cores).  Ties resolve to the lowest centroid index.
- * Requires K <= 1<<20, N < 2^31. */
-size_t fk_assign_workspace_size(int64_t B, int64_t K, int dtype);
+ * 16-bit dtype the chain is round(round(x_sq - round(2*round(x.c))) + c_sq) in
+ * that dtype, overflow to inf included (the centroid operand of the tensor
+ * cores is -2c, staged in the workspace); otherwise float32 (for float32 x
+ * the dot products are 3xTF32 on the tensor cores).  Ties resolve to the
+ * lowest centroid index; a NaN distance wins at its first column, as argmin.
+ * Requires K <= 1<<20, N < 2^31.  The workspace (fk_assign_workspace_size)
+ * holds the padded c_sq and, for 16-bit x, -2c (about B*K*D*2 bytes). */
+size_t fk_assign_workspace_size(int64_t B, int64_t K, int64_t D, int dtype);
 int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
               int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,
               int64_t B, int64_t N, int64_t K, int64_t D, const int64_t* x_strides3,
@@ -181,13 +184,14 @@ int fk_assign_dot_accumulate(const void* x, const void* centroids, int32_t* out,
  * custom-op interface without a workspace hook, a memory pool that forbids side
  * allocations, or a latency-bound loop where cudaMalloc/cudaFree (which can
  * synchronise the device) is not acceptable.  Same arguments and results as
- * fk_assign, minus the workspace: the scratch is a 1 MiB file-scope device
+ * fk_assign, minus the workspace: the scratch is a 16 MiB file-scope device
  * array that every GPU loading this library keeps until exit.
- * Limit: B * ceil(K/256)*256 <= 262080 (e.g. B=32, K <= 8192); larger sizes
- * return FK_ERR_WORKSPACE.  The first call on a device looks the array up
- * (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls on a device share the array (each call rewrites what it reads);
- * calls that overlap on the GPU race on it.  Allocates nothing. */
+ * Limit: fk_assign_workspace_size(B, K, D, dtype) <= 16 MiB (e.g. B=32,
+ * K=1000, D=128 float16 takes 8.3 MiB); larger sizes return FK_ERR_WORKSPACE.
+ * The first call on a device looks the array up (cudaGetSymbolAddress) and
+ * should come before any stream capture.  All calls on a device share the
+ * array (each call rewrites what it reads); calls that overlap on the GPU race
+ * on it.  Allocates nothing. */
 int fk_assign_static_scratch(const void* x, const void* centroids, const void* x_sq,
                              const void* c_sq, int32_t* out, int32_t* counts, int dtype,
                              int xsq_dtype, int csq_dtype, int64_t B, int64_t N, int64_t K,

@@ -11,6 +11,13 @@ The bar (from the project's north star):
 * for the dot-product (cosine / dot k-means) labels the gap is the exact score
   difference ``|x.c_a - x.c_b|`` relative to ``||x|| max(||c_a||, ||c_b||)``,
   with the same tolerances;
+* for 16-bit Euclidean labels a mismatch is also excused as a summation-order
+  tie when the float16 / bfloat16 rounding of a cross product x.c sits so close
+  to a rounding boundary that a float32 sum in another order (bounded by
+  D * 2^-24 * sum|x_i c_i|) rounds it the other way, and with some such
+  rounding the reference's distance chain ranks the kernel's centroid no worse
+  (the chain quantises distances at the unit of x_sq, which for large x_sq is
+  far above the 1e-3 relative bar); these count against the same 0.1 % budget;
 * centroids agree within 1e-3 relative per centroid:
   ``||dc_k|| <= 1e-3 * max(||c_k||, 1e-3 * max_j ||c_j||)``.
 """
@@ -25,9 +32,35 @@ MAX_EXCUSED_FRAC = 1e-3
 CENTROID_RTOL = 1e-3
 
 
-def label_report(x, centroids, got, want, dtype, metric="euclid"):
+def _order_ties(xs, ca, cb, dtype, xsq):
+    """Boolean per row: a float32 summation order of the cross products exists
+    under which the reference's 16-bit chain gives candidate a (the kernel's)
+    a distance no larger than candidate b's (see the module docstring)."""
+    D = xs.shape[-1]
+
+    def chain_range(c):
+        prod = xs * c
+        cross = prod.sum(-1)
+        eps = D * 2.0 ** -24 * np.abs(prod).sum(-1)
+        csq = ko.row_sqnorm(c[None].astype(np.float32), dtype)[0]
+        out = []
+        with np.errstate(all="ignore"):
+            for cr in (cross - eps, cross + eps):
+                rc = ko.round_to(cr, dtype)
+                two = ko.round_to(2.0 * rc, dtype)
+                t = ko.round_to(xsq - two, dtype)
+                out.append(ko.round_to(t + csq, dtype))
+        return np.minimum(*out), np.maximum(*out)
+
+    a_lo, _ = chain_range(ca)
+    _, b_hi = chain_range(cb)
+    return a_lo <= b_hi
+
+
+def label_report(x, centroids, got, want, dtype, metric="euclid", x_sq=None):
     """Compare two labelings of x against centroids; returns a dict.
-    ``metric`` is "euclid" (nearest centroid) or "dot" (largest dot product)."""
+    ``metric`` is "euclid" (nearest centroid) or "dot" (largest dot product);
+    ``x_sq`` (B, N) is the kernel's x_sq in ``dtype`` (default: the oracle's)."""
     got = np.asarray(got).astype(np.int64).reshape(np.asarray(want).shape)
     want = np.asarray(want).astype(np.int64)
     mism = got != want
@@ -52,14 +85,20 @@ def label_report(x, centroids, got, want, dtype, metric="euclid"):
         db = ((xs - cb) ** 2).sum(-1)
         gap = np.abs(da - db) / (np.minimum(np.abs(da), np.abs(db)) + 1e-3)
     tol = LABEL_TOL[dtype]
-    out["excused"] = int((gap < tol).sum())
-    out["bad"] = int((gap >= tol).sum())
+    near = gap < tol
+    order = np.zeros_like(near)
+    if metric == "euclid" and dtype in ("float16", "bfloat16") and (~near).any():
+        xq = ko.row_sqnorm(np.asarray(x, np.float32), dtype) if x_sq is None else np.asarray(x_sq)
+        order = ~near & _order_ties(xs, ca, cb, dtype, np.asarray(xq, np.float64)[bi, ni])
+    out["excused"] = int((near | order).sum())
+    out["order_ties"] = int(order.sum())
+    out["bad"] = int((~(near | order)).sum())
     out["worst_gap"] = float(gap.max())
     return out
 
 
-def assert_labels(x, centroids, got, want, dtype, what="", metric="euclid"):
-    r = label_report(x, centroids, got, want, dtype, metric)
+def assert_labels(x, centroids, got, want, dtype, what="", metric="euclid", x_sq=None):
+    r = label_report(x, centroids, got, want, dtype, metric, x_sq=x_sq)
     assert r["bad"] == 0, f"{what}: {r['bad']} label mismatches beyond near-tie tolerance {r}"
     allowed = max(1, int(np.ceil(MAX_EXCUSED_FRAC * r["n"])))
     assert r["excused"] <= allowed, f"{what}: too many near-tie mismatches {r}"

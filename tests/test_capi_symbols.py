@@ -44,10 +44,13 @@ def test_python_binding_covers_header():
 
 
 def test_host_only_entry_points(lib):
-    assert lib.fk_abi_version() == 1
+    assert lib.fk_abi_version() == 2
     assert lib.fk_status_string(0) == b"ok"
     assert b"workspace" in lib.fk_status_string(3)
-    assert lib.fk_assign_workspace_size(32, 1000, 0) >= 32 * 1024 * 4
+    # padded c_sq, then the -2c operand for 16-bit x (none for float32)
+    assert lib.fk_assign_workspace_size(32, 1000, 128, 0) >= 32 * 1024 * 4 + 32 * 1000 * 128 * 2
+    assert lib.fk_assign_workspace_size(32, 1000, 100, 1) >= 32 * 1024 * 4 + 32 * 1000 * 104 * 2
+    assert lib.fk_assign_workspace_size(32, 1000, 128, 2) < 32 * 1024 * 4 + 1024
     assert lib.fk_centroid_accumulate_workspace_size(32, 75600, 1000) >= 2 * 32 * 75600 * 4
     st = (ctypes.c_int64 * 3)(75600 * 128, 128, 1)
     assert lib.fk_tma_compatible(ctypes.c_void_p(1 << 20), 0, 128, st) == 1

@@ -121,7 +121,7 @@ def test_accumulate_method_matches_workspace(K, D, dt):
     m = lib.fk_assign_accumulate_method(K, D, dt)
     assert m in (nat.FK_ACC_PRIVATISED, nat.FK_ACC_FUSED, nat.FK_ACC_SORTED)
     extra = (lib.fk_assign_accumulate_workspace_size(2, 5000, K, D, dt)
-             - lib.fk_assign_workspace_size(2, K, dt))
+             - lib.fk_assign_workspace_size(2, K, D, dt))
     assert (extra > 0) == (m == nat.FK_ACC_SORTED)
     if m == nat.FK_ACC_FUSED:
         assert dt in (0, 1) and D <= 128

@@ -1,15 +1,13 @@
 """fk_assign_static_scratch: the assignment entry point that allocates nothing.
 
-It serves callers that cannot allocate device memory (a host that only hands
-over inputs and outputs, a pool that forbids side allocations, a loop where
-cudaMalloc's possible device synchronisation is unacceptable).  Its scratch is
-a 1 MiB file-scope device array instead of a caller workspace.  This file is
-named to be collected last so that a run stopping at the first failure has run
-every other test first; it must also pass on its own in a fresh process.
+It serves callers that cannot allocate device memory: a host that hands a
+plugin only its inputs and outputs (no workspace hook), a memory pool that
+forbids side allocations, or a latency-bound loop where cudaMalloc's possible
+device synchronisation is unacceptable.  Its scratch is a 16 MiB file-scope
+device array instead of a caller workspace.  This file is named to be
+collected last so that a run stopping at the first failure has run every
+other test first; it must also pass on its own in a fresh process.
 """
-import ctypes
-
-import numpy as np
 import pytest
 import torch
 
@@ -32,37 +30,73 @@ def _call_static(lib, x, c, xsq, out, status, c_sq=None):
         nat.ptr(status), nat.stream_handle(x.device))
 
 
-@pytest.mark.parametrize("dt,B,N,K,D", [(torch.float16, 4, 6000, 1000, 128),
-                                         (torch.float32, 2, 3000, 300, 96)])
-def test_static_scratch_matches_workspace_entry_point(dt, B, N, K, D):
+NAMES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
+
+
+@pytest.mark.parametrize("dt,B,N,K,D,given_csq", [
+    (torch.float16, 4, 6000, 1000, 128, False),   # 256-column tiles
+    (torch.float16, 3, 5000, 100, 64, False),     # K <= 128: narrow tiles, resident centroids
+    (torch.bfloat16, 2, 3000, 300, 128, True),    # caller-provided c_sq
+    (torch.float32, 2, 3000, 300, 96, False),     # 3xTF32 split-D path
+])
+def test_static_scratch_matches_workspace_entry_point(dt, B, N, K, D, given_csq):
+    """Two calls in a row (the shared scratch is rewritten each time): labels
+    equal fk_assign's with a caller workspace, and agree with the CPU oracle at
+    the parity bar."""
     from flash_kmeans import _native as nat
     from flash_kmeans import _ops
     lib = nat.load()
     g = torch.Generator(device="cuda").manual_seed(11)
     status = torch.zeros(4, dtype=torch.int32, device="cuda")
-    for call in range(2):  # two calls in a row: the shared scratch is rewritten each time
+    name = NAMES[dt]
+    for call in range(2):
         x = torch.randn(B, N, D, device="cuda", generator=g).to(dt)
         c = torch.randn(B, K, D, device="cuda", generator=g).to(dt)
         xsq = _ops.row_sqnorm(x)
-        ref = _ops.assign(x, c, xsq)                      # existing entry point, caller workspace
+        c_sq = _ops.row_sqnorm(c) if given_csq else None
+        ref = _ops.assign(x, c, xsq, c_sq=c_sq)          # existing entry point, caller workspace
         got = torch.full((B, N), -1, dtype=torch.int32, device="cuda")
-        rc = _call_static(lib, x, c, xsq, got, status)
-        nat.check(rc, "fk_assign_static_scratch")
+        nat.check(_call_static(lib, x, c, xsq, got, status, c_sq=c_sq), "fk_assign_static_scratch")
         torch.cuda.synchronize()
         assert int(status[0]) == 0
-        name = "float16" if dt == torch.float16 else "float32"
-        assert_labels(x.float().cpu().numpy(), c.float().cpu().numpy(), got.cpu().numpy(),
-                      ref.cpu().numpy(), name, f"static scratch call {call}")
         assert torch.equal(got, ref), f"call {call}: labels differ from fk_assign"
+        xn, cn = x.float().cpu().numpy(), c.float().cpu().numpy()
+        o = ko.assign(xn, cn, xsq.float().cpu().numpy(), name)
+        assert_labels(xn, cn, got.cpu().numpy(), o, name, f"static scratch call {call} vs oracle")
+
+
+def test_static_scratch_allocates_nothing():
+    """After the first call (which loads the library's device module, static
+    array included), further calls leave the device's free memory unchanged."""
+    from flash_kmeans import _native as nat
+    from flash_kmeans import _ops
+    lib = nat.load()
+    B, N, K, D = 8, 4000, 512, 128
+    x = torch.randn(B, N, D, device="cuda").half()
+    c = torch.randn(B, K, D, device="cuda").half()
+    xsq = _ops.row_sqnorm(x)
+    out = torch.empty((B, N), dtype=torch.int32, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    nat.check(_call_static(lib, x, c, xsq, out, status), "fk_assign_static_scratch")
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        nat.check(_call_static(lib, x, c, xsq, out, status), "fk_assign_static_scratch")
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert int(status[0]) == 0
 
 
 def test_static_scratch_rejects_oversize_without_launch():
     from flash_kmeans import _native as nat
     lib = nat.load()
-    x = torch.zeros(2, 8, 128, dtype=torch.float16, device="cuda")
-    c = torch.zeros(2, 131_072, 128, dtype=torch.float16, device="cuda")  # B*Kpad = 262144 > 262080
-    xsq = torch.zeros(2, 8, dtype=torch.float16, device="cuda")
-    out = torch.full((2, 8), -7, dtype=torch.int32, device="cuda")
+    B, K, D = 32, 2048, 128   # c_sq 256 KiB + -2c 16 MiB > 16 MiB
+    assert lib.fk_assign_workspace_size(B, K, D, nat.FK_F16) > (16 << 20)
+    x = torch.zeros(B, 8, D, dtype=torch.float16, device="cuda")
+    c = torch.zeros(B, K, D, dtype=torch.float16, device="cuda")
+    xsq = torch.zeros(B, 8, dtype=torch.float16, device="cuda")
+    out = torch.full((B, 8), -7, dtype=torch.int32, device="cuda")
     status = torch.zeros(4, dtype=torch.int32, device="cuda")
     rc = _call_static(lib, x, c, xsq, out, status)
     assert rc == 3  # FK_ERR_WORKSPACE
