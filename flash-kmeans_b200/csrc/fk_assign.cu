@@ -78,12 +78,21 @@ struct Layout {
   static constexpr int kGroups = EPI / 4;  // column groups of each centroid tile
   static constexpr int kSplit = split_mode(MODE) ? 2 : 1;  // hi/lo copies for 3xTF32
   static constexpr int kCChunk = KC * kChunkB;        // one 128-byte column chunk of a tile
-  static constexpr int kAcc = kTmemCols / KC;          // TMEM accumulators
+  // Fused accumulation comes in two forms: with 256-column tiles (large K)
+  // four sum warps add each point's row to its cluster's sums with vector
+  // atomics; with 128-column tiles (K <= 128) the tensor core adds a one-hot
+  // matrix times the tile's x into a TMEM sums accumulator (kOneHot).
+  static constexpr bool kOneHot = FUSE && KC < kCent;
+  static constexpr bool kSumWarps = FUSE && !kOneHot;
+  // TMEM accumulators (the one-hot form keeps 128 columns for the sums)
+  static constexpr int kAcc = kOneHot ? (kTmemCols - 128) / KC : kTmemCols / KC;
+  static constexpr int kSumsCol = kAcc * KC;            // first TMEM column of the sums
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
   // or (narrow tiles, one centroid tile per point tile) lets x loads run
   // further ahead of the short per-tile MMA work; with resident centroids
-  // (RESC) the ring is small and five x tiles fit
-  static constexpr int XB = RESC ? 5 : ((FUSE || KC < kCent) ? 3 : 2);
+  // (RESC) the ring is small and five x tiles fit (three next to the one-hot
+  // buffers)
+  static constexpr int XB = RESC ? (kOneHot ? 3 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -92,11 +101,17 @@ struct Layout {
   static constexpr int st_xlo = st_x + kXChunk;           // x chunk lo (mode 2)
   static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
-  static constexpr int merge_off = stages_off + STAGES * stage_bytes;
+  // one-hot operands [parity][point chunk 0..1][centroid row][64 points], 16-bit,
+  // 128-byte swizzle (K-major A operand of the sums MMA)
+  static constexpr int oh_off = stages_off + STAGES * stage_bytes;
+  static constexpr int oh_bytes = kOneHot ? 2 * 2 * kXChunk : 0;
+  static constexpr int hist_off = oh_off + oh_bytes;          // per-CTA counts, K <= 128
+  static constexpr int hist_bytes = kOneHot ? 128 * 4 : 0;
+  static constexpr int merge_off = hist_off + hist_bytes;
   // [parity][group 1..G-1][row] (value, index) candidates for the merge
   static constexpr int merge_bytes = 2 * (kGroups - 1) * kRows * 8;
   static constexpr int lab_off = merge_off + merge_bytes;
-  static constexpr int lab_bytes = FUSE ? 2 * kRows * 4 : 0;  // [parity][row] label or -1
+  static constexpr int lab_bytes = kSumWarps ? 2 * kRows * 4 : 0;  // [parity][row] label or -1
   // modes 0, 3, 4: each epilogue thread's saved chunk (16 packed distances,
   // or 16 float32 scores), as [unit 0..3][epilogue thread] 16-byte units
   // (conflict-free stores)
@@ -106,17 +121,18 @@ struct Layout {
   static constexpr int bar_off = save_off + save_bytes;
   // x_full[XB] x_empty[XB] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
-  static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1;
+  // oh_full[2] oh_empty[2] sums_full[1] sums_empty[1] fl_ready[1] fl_done[1]
+  static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1 + 8;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
-  static constexpr bool kExtra = split_mode(MODE) || FUSE;  // warpgroup 3
+  static constexpr bool kExtra = split_mode(MODE) || kSumWarps;  // warpgroup 3
   static constexpr int threads = (kEpiWarp0 + EPI + (kExtra ? kConvWarps : 0)) * 32;
   // Register budgets (setmaxnreg).  kLaunchRegs is what ptxas gives a thread
   // under __launch_bounds__(threads, 1); the host checks the kernel's actual
   // count before launching.  Control warps shrink to kCtlRegs, the extra
   // warpgroup to kExtraRegs, and the epilogue takes the rest.
   static constexpr int kLaunchRegs = threads == 384 ? 168 : 128;
-  static constexpr int kCtlRegs = 72;
+  static constexpr int kCtlRegs = kOneHot ? 96 : 72;
   static constexpr int kExtraRegs = FUSE ? 96 : 72;
   static constexpr int kEpiRegs =
       ((threads * kLaunchRegs - 128 * kCtlRegs - (kExtra ? 128 * kExtraRegs : 0)) / (EPI * 32)) & ~7;
@@ -210,6 +226,7 @@ struct Pack2;
 template <>
 struct Pack2<__half> {
   FK_PACK2_OPS("f16x2", 0x7C007C00u)
+  static constexpr unsigned short kOne = 0x3C00;  // 1.0
   __device__ __forceinline__ static float lo(uint32_t v) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
   }
@@ -225,6 +242,7 @@ struct Pack2<__half> {
 template <>
 struct Pack2<__nv_bfloat16> {
   FK_PACK2_OPS("bf16x2", 0x7F807F80u)
+  static constexpr unsigned short kOne = 0x3F80;  // 1.0
   __device__ __forceinline__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
   __device__ __forceinline__ static float hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
   __device__ __forceinline__ static uint32_t splat(float v) {
@@ -489,6 +507,12 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   uint64_t* lab_full = merge_empty + 2;
   uint64_t* lab_empty = lab_full + 2;
   uint64_t* final_bar = lab_empty + 2;
+  uint64_t* oh_full = final_bar + 1;     // one-hot operand of a tile written (128 points)
+  uint64_t* oh_empty = oh_full + 2;      // its sums MMAs done (buffer and x tile free)
+  uint64_t* sums_full = oh_empty + 2;    // a batch's sums complete in TMEM
+  uint64_t* sums_empty = sums_full + 1;  // the epilogue has added them to global memory
+  uint64_t* fl_ready = sums_empty + 1;   // epilogue warps done with a batch's last tile
+  uint64_t* fl_done = fl_ready + 1;      // the batch's sums and counts added, counts reset
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
 
@@ -497,7 +521,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       mbar_init(&x_full[i], 1);
       // with FUSE the resident x tile is also read by the 128 sum threads
       // (the points' rows) before it may be overwritten
-      mbar_init(&x_empty[i], FUSE ? 1 + 128 : 1);
+      mbar_init(&x_empty[i], L::kSumWarps ? 1 + 128 : 1);
     }
     for (int i = 0; i < kAcc; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -515,8 +539,25 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       mbar_init(&conv_full[s], kConvWarps * 32);
     }
     mbar_init(final_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&oh_full[i], 128);
+      mbar_init(&oh_empty[i], 1);
+    }
+    mbar_init(sums_full, 1);
+    mbar_init(sums_empty, kEpiWarps * 32);
+    mbar_init(fl_ready, kEpiWarps * 32);
+    mbar_init(fl_done, kEpiWarps * 32);
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if constexpr (L::kOneHot) {
+    // one-hot buffers start all zero (each tile then sets one element per
+    // point and clears the element it set two tiles earlier); counts zero
+    uint4* oh = reinterpret_cast<uint4*>(smem + L::oh_off);
+    for (int i = threadIdx.x; i < L::oh_bytes / 16; i += blockDim.x) oh[i] = make_uint4(0, 0, 0, 0);
+    int* hist = reinterpret_cast<int*>(smem + L::hist_off);
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) hist[i] = 0;
+    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -621,6 +662,50 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       uint32_t aph = 0;
       int bi = -1, prev_b = -1;  // RESC: as in the producer
       bool ok = true;
+      // One-hot accumulation: the sums MMAs of tile t run after the assignment
+      // MMAs of tile t+1 (the epilogue needs the labels of t first):
+      // sums[k][d] += sum_p onehot[k][p] * x[p][d] into the TMEM sums columns,
+      // A = one-hot (K-major: points contiguous per centroid), B = the tile's
+      // x buffer read MN-major (dims contiguous per point; LBO = the 64-dim
+      // chunk stride, SBO = 8 points).  A batch's last tile commits sums_full;
+      // the next batch's first sums MMA waits until the epilogue has read them.
+      int pt = -1, pxb = 0;       // tile whose sums MMAs are pending, its x buffer
+      int ohn = 0, fln = 0;       // one-hot buffers consumed, flushes done
+      bool sums_on = false;       // the current batch's sums already started
+      auto sums_mma = [&](int tt, int xbuf) -> bool {
+        if constexpr (L::kOneHot) {
+          constexpr uint32_t idesc_s = instr_desc(Elem<T>::kMmaFmt, kRows, 128) | (1u << 16);
+          if (!sums_on && fln > 0) {
+            if (!mbar_wait(sums_empty, static_cast<uint32_t>((fln - 1) & 1), abort_flag, p.status,
+                           FK_DEV_WAIT_TIMEOUT))
+              return false;
+            tc_fence_after();
+          }
+          const int par = ohn & 1;
+          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn >> 1) & 1), abort_flag,
+                         p.status, FK_DEV_WAIT_TIMEOUT))
+            return false;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + L::oh_off + par * 2 * kXChunk);
+          const uint32_t b0 = smem_u32(smem + L::x_off + xbuf * kResidentChunks * kXChunk);
+#pragma unroll
+          for (int s = 0; s < 8; ++s)   // 16 points per MMA
+            mma_f16(tmem_base + static_cast<uint32_t>(L::kSumsCol),
+                    smem_desc_sw128(a0 + (s >> 2) * kXChunk + (s & 3) * 32),
+                    smem_desc_sw128_mn(b0 + s * 16 * kChunkB, kXChunk, 1024), idesc_s,
+                    (sums_on || s > 0) ? 1u : 0u);
+          sums_on = true;
+          mma_commit(&oh_empty[par]);
+          mma_commit(&x_empty[xbuf]);
+          ++ohn;
+          if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
+            mma_commit(sums_full);
+            ++fln;
+            sums_on = false;
+          }
+        }
+        return true;
+      };
       for (int t = t_begin; ok && t < t_end; ++t) {
         bool new_batch = false, last_of_batch = false;
         if constexpr (RESC) {
@@ -693,10 +778,22 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
         if constexpr (XRES) {
           if (ok) {
-            mma_commit(&x_empty[xb]);
+            if constexpr (L::kOneHot) {
+              if (pt >= 0 && !sums_mma(pt, pxb)) {
+                ok = false;
+                break;
+              }
+              pt = t;
+              pxb = xb;
+            } else {
+              mma_commit(&x_empty[xb]);
+            }
             if (++xb == L::XB) { xb = 0; xph ^= 1; }
           }
         }
+      }
+      if constexpr (L::kOneHot) {
+        if (ok && pt >= 0) ok = sums_mma(pt, pxb);
       }
       // All MMAs this thread issued must finish before TMEM is released.
       mma_commit(final_bar);
@@ -717,6 +814,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     uint32_t aph = 0;
     int it = 0;
     bool ok = true;
+    int prev_lab[2] = {-1, -1};  // one-hot: the element this point set in each buffer
+    int fln = 0;                 // one-hot: batch flushes done
     // x_sq of this thread's point in tile t (0 past N), fetched one tile
     // ahead so the tile's first distances do not wait on an HBM read
     auto load_xsq = [&](int t) -> float {
@@ -895,9 +994,34 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         mbar_arrive(&merge_empty[par]);
         if (valid) {
           p.out[b * p.so_b + static_cast<int64_t>(n) * p.so_n] = idx;
-          if (p.counts) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
+          if (p.counts && !L::kOneHot) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
         }
-        if constexpr (FUSE && XRES) {
+        if constexpr (L::kOneHot) {
+          // count the point (warp-aggregated shared atomics), then mark it in
+          // this tile's one-hot buffer: clear the element it set two tiles ago,
+          // set (label, point) to 1
+          const int lab = valid ? idx : -1;
+          const unsigned grp = __match_any_sync(0xffffffffu, lab);
+          if (lab >= 0 && lane == __ffs(grp) - 1)
+            atomicAdd(reinterpret_cast<int*>(smem + L::hist_off) + lab, __popc(grp));
+          const bool got2 = mbar_wait(&oh_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got2)) {
+            ok = false;
+            break;
+          }
+          uint8_t* ob = smem + L::oh_off + par * 2 * kXChunk + (row >> 6) * kXChunk;
+          const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
+          auto elem = [&](int k) -> unsigned short* {
+            return reinterpret_cast<unsigned short*>(
+                ob + k * kChunkB + ((((pb >> 4) ^ (k & 7))) << 4) + (pb & 15));
+          };
+          if (prev_lab[par] >= 0) *elem(prev_lab[par]) = 0;
+          if (lab >= 0) *elem(lab) = Pack2<T>::kOne;
+          prev_lab[par] = lab;
+          fence_proxy_async_smem();
+          mbar_arrive(&oh_full[par]);
+        }
+        if constexpr (L::kSumWarps && XRES) {
           // hand the label (or -1 past N) to the sum warps
           const bool got2 = mbar_wait(&lab_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
           if (!__all_sync(0xffffffffu, got2)) {
@@ -908,8 +1032,56 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           mbar_arrive(&lab_full[par]);
         }
       }
+      if constexpr (L::kOneHot) {
+        // a batch's last tile in this CTA: add the TMEM sums (lanes = centroids,
+        // this warp's 64 of the 128 dimension columns) and the shared counts to
+        // the global accumulators, reset the counts
+        if (t + 1 == t_end || (t + 1) / p.ntn != b) {
+          const uint32_t fph = static_cast<uint32_t>(fln & 1);
+          mbar_arrive(fl_ready);
+          bool got3 = mbar_wait(fl_ready, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          got3 = got3 && mbar_wait(sums_full, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t sa[32], sb[32];
+          const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                              static_cast<uint32_t>(L::kSumsCol + h * 64);
+          tmem_ld32(ta, sa);
+          tmem_ld32(ta + 32, sb);
+          tmem_ld_wait(sa);
+          tmem_ld_wait(sb);
+          tc_fence_before();
+          mbar_arrive(sums_empty);
+          const int k = q * 32 + lane;   // this thread's centroid
+          if (k < p.K) {
+            float* dst = p.sums + (static_cast<int64_t>(b) * p.K + k) * p.D;
+            const int d0 = h * 64;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (d0 + j < p.D) atomicAdd(dst + d0 + j, __uint_as_float(sa[j]));
+              if (d0 + 32 + j < p.D) atomicAdd(dst + d0 + 32 + j, __uint_as_float(sb[j]));
+            }
+            if (h == 0) {
+              int* hist = reinterpret_cast<int*>(smem + L::hist_off);
+              const int c = hist[k];
+              if (c) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + k, c);
+              hist[k] = 0;
+            }
+          }
+          mbar_arrive(fl_done);
+          const bool got4 = mbar_wait(fl_done, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got4)) {
+            ok = false;
+            break;
+          }
+          ++fln;
+        }
+      }
     }
-  } else if (FUSE && XRES) {
+  } else if (L::kSumWarps && XRES) {
     // ------------------------------------------- sum warps (fused accumulation)
     // Sum warp w adds rows 32w..32w+31 of every tile, one point at a time:
     // lane l takes columns 4l..4l+3 of the point's row (still resident in the
@@ -921,7 +1093,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     // it releases the x buffer.  Runs concurrently with the next tile's
     // epilogue.
     if constexpr (L::kExtraRegs < L::kLaunchRegs) setmaxnreg_dec<L::kExtraRegs>();
-    if constexpr (FUSE && XRES && sizeof(T) == 2) {
+    if constexpr (L::kSumWarps && XRES && sizeof(T) == 2) {
     const int sw = warp - kConvWarp0;  // 0..3
     const int col = 4 * lane;
     const int dc = col / p.dch;
@@ -1145,7 +1317,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   const bool xres = is16 && nd <= kResidentChunks;
   // K <= 128 (one centroid tile either way): 128-column tiles, so the epilogue
   // skips the padding half of a 256-column tile and TMEM holds four accumulators
-  const bool narrow = is16 && !sums && K <= kCent / 2;
+  // (with fused sums the narrow kernel accumulates them on the tensor core)
+  const bool narrow = is16 && K <= kCent / 2;
   const int kc = narrow ? kCent / 2 : kCent;
   const int nkt = static_cast<int>((K + kc - 1) / kc);
   const int64_t kpad = static_cast<int64_t>(nkt) * kc;
@@ -1225,7 +1398,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
     if constexpr (Elem<T>::kBytes == 2) {
       if (sums) {
         if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
-        return launch_assign<T, 3, true, true>(tx, tc, p, stream);
+        return narrow ? launch_assign<T, 3, true, true, kCent / 2, true>(tx, tc, p, stream)
+                      : launch_assign<T, 3, true, true>(tx, tc, p, stream);
       }
       if (narrow)
         return xres ? launch_assign<T, 3, true, false, kCent / 2, true>(tx, tc, p, stream)
@@ -1240,6 +1414,9 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   if constexpr (Elem<T>::kBytes == 2) {
     if (sums) {  // fused centroid sums: resident x tiles only (checked by the caller)
       if (!xres) return fail(FK_ERR_UNSUPPORTED, "fused sums need a resident x tile");
+      if (narrow)  // K <= 128: one-hot sums on the tensor core
+        return mode == 0 ? launch_assign<T, 0, true, true, kCent / 2, true>(tx, tc, p, stream)
+                         : launch_assign<T, 1, true, true, kCent / 2, true>(tx, tc, p, stream);
       return mode == 0 ? launch_assign<T, 0, true, true>(tx, tc, p, stream)
                        : launch_assign<T, 1, true, true>(tx, tc, p, stream);
     }
@@ -1363,31 +1540,44 @@ extern "C" int fk_assign_dot(const void* x, const void* centroids, int32_t* out,
 // histogram followed by fk_centroid_accumulate (counting-sort path).
 // ---------------------------------------------------------------------------
 // How fk_assign_accumulate accumulates:
-//   privatised: K x D small enough for shared memory; fk_assign (labels only)
-//     then the privatised segmented sum, which reads x a second time but adds
-//     each CTA's partial sums to the global ones once (with small K the fused
-//     kernel's per-point atomics would pile onto a few cluster rows);
-//   fused: 16-bit x with D <= 128, the sum warps of the assignment kernel add
-//     each point's resident row (x read once);
+//   fused (16-bit x with D <= 128, x read once): with K <= 128 the narrow
+//     assignment kernel also multiplies each tile's one-hot label matrix with
+//     the resident x tile on the tensor core into TMEM sums, added to the
+//     global sums once per batch and CTA; with larger K, when a batch's K x D
+//     float32 sums do not fit in shared memory, the sum warps of the
+//     assignment kernel add each point's resident row with vector atomics;
+//   privatised: K x D small enough for shared memory otherwise; fk_assign
+//     (labels only) then the privatised segmented sum, which reads x a second
+//     time but adds each CTA's partial sums to the global ones once;
 //   sorted: otherwise fk_assign then fk_centroid_accumulate's counting sort.
-static bool assign_accumulate_priv(int64_t K, int64_t D) { return segsum_priv_fits(K, D); }
-
-static bool assign_accumulate_fused(int64_t K, int64_t D, int dtype) {
-  if (assign_accumulate_priv(K, D)) return false;
+// 16-bit x whose tile stays resident in shared memory (D <= 128)
+static bool assign_accumulate_resident16(int64_t D, int dtype) {
   if (dtype != FK_F16 && dtype != FK_BF16) return false;
   const int64_t nd = (D * 2 + kChunkB - 1) / kChunkB;
   return nd <= kResidentChunks;
 }
 
+// fused: one kernel reads x once; with K <= 128 the sums are a one-hot
+// product on the tensor core, otherwise (when a batch's K x D sums do not fit
+// in shared memory) the sum warps add rows with vector atomics
+static bool assign_accumulate_fused(int64_t K, int64_t D, int dtype) {
+  if (!assign_accumulate_resident16(D, dtype)) return false;
+  return K <= kCent / 2 || !segsum_priv_fits(K, D);
+}
+
+static bool assign_accumulate_priv(int64_t K, int64_t D, int dtype) {
+  return !assign_accumulate_fused(K, D, dtype) && segsum_priv_fits(K, D);
+}
+
 extern "C" int fk_assign_accumulate_method(int64_t K, int64_t D, int dtype) {
-  if (assign_accumulate_priv(K, D)) return FK_ACC_PRIVATISED;
-  return assign_accumulate_fused(K, D, dtype) ? FK_ACC_FUSED : FK_ACC_SORTED;
+  if (assign_accumulate_fused(K, D, dtype)) return FK_ACC_FUSED;
+  return assign_accumulate_priv(K, D, dtype) ? FK_ACC_PRIVATISED : FK_ACC_SORTED;
 }
 
 extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                       int dtype) {
   const size_t wa = fk_assign_workspace_size(B, K, D, dtype);
-  if (assign_accumulate_priv(K, D) || assign_accumulate_fused(K, D, dtype)) return wa;
+  if (assign_accumulate_priv(K, D, dtype) || assign_accumulate_fused(K, D, dtype)) return wa;
   return wa + align_up(static_cast<size_t>(B > 0 && K > 0 ? B * K : 1) * 4, 256) +
          fk_centroid_accumulate_workspace_size(B, N, K);
 }
@@ -1415,7 +1605,7 @@ static int assign_accumulate_entry(const char* fn, bool dot, const void* x, cons
                         N, K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2,
                         workspace, ws_bytes, dev_status, stream);
   };
-  if (assign_accumulate_priv(K, D)) {
+  if (assign_accumulate_priv(K, D, dtype)) {
     int st = assign(nullptr, workspace_bytes);
     if (st != FK_OK) return st;
     return segsum_priv(x, dtype, x_strides3, out, FK_I32, out_strides2, B, N, K, D, sums, counts,

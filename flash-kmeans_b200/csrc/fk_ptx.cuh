@@ -239,7 +239,23 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor, dense, f32 accumulator, both operands K-major.
+// Shared-memory matrix descriptor for an MN-major operand stored with the
+// 128-byte swizzle: each 128-byte row holds 64 consecutive MN elements (16-bit)
+// of one K index, 8 K rows form a 1024-byte atom; `lbo` = byte stride between
+// 64-element groups along MN, `sbo` = byte stride between 8-row groups along K.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo,
+                                                       uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor, dense, f32 accumulator, both operands K-major
+// (bit 15 / 16 set afterwards make A / B MN-major).
 // ab_fmt: 0 = f16, 1 = bf16, 2 = tf32.
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_fmt, uint32_t M, uint32_t N) {
   return (1u << 4)              // D format f32

@@ -255,9 +255,9 @@ def test_accumulate_privatised_and_sorted_paths(fk, dt, B, N, K, D, idt):
     ("float16", 64, 1000, 100, 128), ("bfloat16", 40, 700, 17, 64),
     ("float16", 1, 300000, 128, 128), ("float16", 3, 129, 1, 8), ("float16-xsq32", 5, 3000, 60, 128)])
 def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
-    """fk_assign_accumulate (privatised for small K x D, fused for 16-bit D<=128, sorted
-    otherwise) equals fk_assign + torch index_add: labels bit-identical, counts exact, sums
-    to fp32 order."""
+    """fk_assign_accumulate (fused for 16-bit D<=128: one-hot tensor-core sums for K<=128,
+    sum warps for larger K; privatised or sorted otherwise) equals fk_assign + torch
+    index_add: labels bit-identical, counts exact, sums to fp32 order."""
     from flash_kmeans import _native as nat
     from flash_kmeans import _ops
     lib = nat.load()

@@ -310,9 +310,9 @@ def test_cosine_engine_launch_count_and_no_allocation(fk):
 @pytest.mark.parametrize("dt,B,N,K,D", [
     ("float16", 2, 20000, 1000, 128),    # fused sums in the assignment kernel
     ("bfloat16", 1, 30000, 1000, 64),    # fused, D = 64
-    ("float16", 3, 9000, 128, 128),      # privatised sum, narrow tiles
-    ("bfloat16", 1, 7000, 50, 100),      # privatised, D = 100
-    ("float16", 50, 900, 64, 64),        # privatised, many batches
+    ("float16", 3, 9000, 128, 128),      # fused one-hot sums, narrow tiles
+    ("bfloat16", 1, 7000, 50, 100),      # fused one-hot, D = 100
+    ("float16", 50, 900, 64, 64),        # fused one-hot, many batches (one flush each)
     ("float16", 1, 3000, 200, 192),      # privatised, split-D
     ("float16", 1, 5000, 2000, 192),     # sorted (D > 128)
     ("float32", 2, 4000, 700, 96),       # sorted, float32
