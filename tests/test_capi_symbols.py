@@ -109,7 +109,7 @@ def test_accumulate_method_codes_are_stable(lib):
     assert (_native.FK_ACC_PRIVATISED, _native.FK_ACC_FUSED, _native.FK_ACC_SORTED) == (0, 1, 2)
     # K <= 128 with 16-bit x and D <= 128: one kernel, one-hot sums on the tensor core
     assert lib.fk_assign_accumulate_method(128, 128, 0) == _native.FK_ACC_FUSED
-    assert lib.fk_assign_accumulate_method(300, 128, 0) == _native.FK_ACC_PRIVATISED
+    assert lib.fk_assign_accumulate_method(200, 128, 0) == _native.FK_ACC_PRIVATISED
     assert lib.fk_assign_accumulate_method(128, 128, 2) == _native.FK_ACC_PRIVATISED
     assert lib.fk_assign_accumulate_method(1000, 128, 0) == _native.FK_ACC_FUSED
     assert lib.fk_assign_accumulate_method(1024, 2048, 2) == _native.FK_ACC_SORTED
