@@ -7,10 +7,12 @@ assignment + update + shift per iteration, ``break`` when the shift drops
 below ``tol`` (returning the centroids that produced the last labels), and the
 result ``(cluster_ids int32 (B,N), centroids (B,K,D) x.dtype, n_iters)``.
 
-Per iteration the B200 build launches fk_assign_accumulate (labels, and the
-points' rows and counts added to the per-cluster sums in the same pass over x)
-and fk_centroid_finalize (means, next ||c||^2, shift, and zeroing of the
-accumulators for the next iteration) -- no memsets, x read once.  The host reads the 8-byte
+Per iteration the B200 build launches fk_assign_accumulate (the centroid
+operand and c_sq staged by one small kernel, then labels with the points' rows
+and counts added to the per-cluster sums in the same pass over x whenever x is
+16-bit with D <= 128) and fk_centroid_finalize (means, next ||c||^2, shift),
+whose two stream-ordered memsets zero the accumulators for the next
+iteration.  The host reads the 8-byte
 (shift, status) record only when ``tol > 0`` or ``verbose`` needs it; with
 ``tol <= 0`` the shift can never be below tol, so iterations are queued back
 to back with no host synchronisation.

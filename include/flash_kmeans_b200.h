@@ -7,9 +7,11 @@
  * (`stream` is a cudaStream_t; NULL means the legacy default stream) and never
  * synchronises.  Buffers are caller-owned; scratch memory is the caller's
  * `workspace` (size from the matching *_workspace_size query).  Nothing is
- * allocated and no global mutable state is kept apart from one-time lookups
- * (driver entry point, per-device SM count, kernel attributes), so one host
- * thread may drive several devices by switching the current device.
+ * allocated.  Global mutable state: one-time per-device lookups (driver entry
+ * point, SM count, kernel attributes, the address of fk_assign_static_scratch's
+ * array), all thread-safe, and that 16 MiB static array itself, which only
+ * fk_assign_static_scratch uses (its calls share it).  One host thread may
+ * drive several devices by switching the current device.
  *
  * Errors: functions return FK_OK (0) or an fk_status code; fk_last_error()
  * returns a thread-local message for the last failure.  Kernels that can
