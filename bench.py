@@ -655,12 +655,36 @@ def _largeN_parity(rank, world, dev, pg):
             "centroid_max_rel_diff": float(t[1]), "ok": int(t[0]) == 0 and float(t[1]) <= 1e-5}
 
 
+def _bind_to_gpu_cpus(dev):
+    """Run this process on the CPUs NVML reports as local to its GPU, so that
+    pinned host memory allocated afterwards lands on the GPU's NUMA node
+    (first touch).  Returns the number of CPUs bound to, or None."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+        cpus &= set(range(os.cpu_count()))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:
+        pass
+    return None
+
+
 def large_n_record(rank, world, dev):
     """The out-of-core record of the default bench line (see the module
-    docstring); every rank takes part, rank 0's dict is printed."""
+    docstring); every rank takes part, rank 0's dict is printed.  With several
+    ranks each binds to its GPU's local CPUs first (host-memory placement)."""
     import torch.distributed as dist
     pg = dist.group.WORLD if world > 1 else None
-    rec = {"config5": _largeN_point(LARGE_N, rank, world, dev, pg)}
+    bound = _bind_to_gpu_cpus(dev) if world > 1 else None
+    rec = {"config5": _largeN_point(LARGE_N, rank, world, dev, pg),
+           "rank0_cpus_bound": bound}
     rec["parity"] = _largeN_parity(rank, world, dev, pg)
     rec["config5_2e28"] = _largeN_big(rank, world, dev, pg)
     rec["note"] = ("speed-up over 1 GPU = ms_per_iter at N=1 / ms_per_iter here (the N=1 line "
