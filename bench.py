@@ -303,6 +303,23 @@ def _load_traffic(name):
         return None
 
 
+def _roofline(hbm_bound, tflops, alg_bytes, ms, burst, sustained, hbm, src, traffic):
+    """The binding roofline of the assignment launch: the tensor pipe when its
+    FLOPs take longer at the measured GEMM peak than its algorithmic bytes at the
+    measured copy bandwidth (configs 2 and 4), else HBM (config 3: K=128 gives
+    128 FLOPs per byte of x, below the ridge)."""
+    if hbm_bound:
+        gbs = alg_bytes / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(gbs / hbm, 4), "peak_source": f"{src} copy bandwidth, per GPU",
+                "algorithmic_bytes": int(alg_bytes), "tensor_tflops": round(tflops, 2),
+                "traffic": traffic}
+    return {"bound": "tensor", "achieved": round(tflops, 2), "peak": burst, "unit": "TFLOP/s",
+            "frac": round(tflops / burst, 4), "peak_source": f"{src} dense bf16 (burst), per GPU",
+            "frac_of_sustained": round(tflops / sustained, 4) if sustained else None,
+            "algorithmic_bytes": int(alg_bytes), "traffic": traffic}
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -391,6 +408,11 @@ def run_ours(args, rank, world, local_rank):
     value = flops / (ms * 1e-3) / 1e12
     burst, sustained, hbm, src = _peaks()
     achieved = flops_rank / (assign_ms * 1e-3) / 1e12
+    # algorithmic DRAM bytes of one assignment launch on this rank: x, x_sq and
+    # the centroids read once, labels and float32 sums written once
+    alg_bytes = sum(t.numel() * t.element_size() for t in (eng.x, eng.x_sq, eng.c_cur, eng.ids)
+                    if t is not None) + eng.sums.numel() * 4
+    hbm_bound = alg_bytes / (hbm * 1e9) > flops_rank / (burst * 1e12)
 
     # ---- e2e through the public API with host buffers (each rank its batches)
     e2e = None
@@ -469,11 +491,8 @@ def run_ours(args, rank, world, local_rank):
                        "step": "one Lloyd iteration incl. the per-iteration shift readback"},
             "ms_per_iter": round(ms, 4),
             "assign_ms": round(assign_ms, 4),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst,
-                         "unit": UNIT, "frac": round(achieved / burst, 4),
-                         "peak_source": f"{src} dense bf16 (burst), per GPU",
-                         "frac_of_sustained": round(achieved / sustained, 4) if sustained else None,
-                         "traffic": None if sim else _load_traffic(args.workload)},
+            "roofline": _roofline(hbm_bound, achieved, alg_bytes, assign_ms, burst, sustained, hbm,
+                                  src, None if sim else _load_traffic(args.workload)),
             "e2e": e2e,
             "cpu_baseline": cpu_baseline,
             "large_n": large_n,
@@ -744,7 +763,9 @@ def run_assign(args, rank, world, local_rank):
     ms = float(t[0])
     flops = _flops(w)
     achieved = flops / (ms * 1e-3) / 1e12
-    burst, sustained, _, src = _peaks()
+    burst, sustained, hbm, src = _peaks()
+    alg_bytes = sum(t.numel() * t.element_size() for t in (x, x_sq, c0, out))
+    hbm_bound = alg_bytes / (hbm * 1e9) > flops / (burst * 1e12)
     if rank == 0:
         print(json.dumps({
             "metric": "assign TFLOP/s (euclid_assign_triton, labels only)",
@@ -756,10 +777,8 @@ def run_assign(args, rank, world, local_rank):
             "config": {"workload": _describe(args.workload, w),
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "step": "one euclid_assign_triton call (c_sq staging + assignment)"},
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst,
-                         "unit": UNIT, "frac": round(achieved / burst, 4),
-                         "peak_source": f"{src} dense bf16 (burst)",
-                         "traffic": _load_traffic(f"plain_{args.workload}")},
+            "roofline": _roofline(hbm_bound, achieved, alg_bytes, ms, burst, sustained, hbm, src,
+                                  _load_traffic(f"plain_{args.workload}")),
             "gpu_launches": 2 * args.steps,
             "clocks": clk.summary(),
         }), flush=True)
