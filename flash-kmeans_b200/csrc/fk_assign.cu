@@ -90,9 +90,10 @@ struct Layout {
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
   // or (narrow tiles, one centroid tile per point tile) lets x loads run
   // further ahead of the short per-tile MMA work; with resident centroids
-  // (RESC) the ring is small and five x tiles fit (three next to the one-hot
-  // buffers)
-  static constexpr int XB = RESC ? (kOneHot ? 3 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
+  // (RESC) the ring is small and five x tiles fit (four next to the one-hot
+  // buffer: a one-hot tile holds its x buffer until its sums MMAs finish, so
+  // the ring must cover the load latency plus two epilogue periods)
+  static constexpr int XB = RESC ? (kOneHot ? 4 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -101,10 +102,14 @@ struct Layout {
   static constexpr int st_xlo = st_x + kXChunk;           // x chunk lo (mode 2)
   static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
-  // one-hot operands [parity][point chunk 0..1][centroid row][64 points], 16-bit,
-  // 128-byte swizzle (K-major A operand of the sums MMA)
+  // one-hot operand [point chunk 0..1][centroid row][64 points], 16-bit,
+  // 128-byte swizzle (K-major A operand of the sums MMA).  One buffer: the
+  // epilogue of tile t writes it after the sums MMAs of tile t-1 (issued right
+  // after the assignment MMAs of tile t) have finished, by which time it has
+  // reduced the whole tile.
+  static constexpr int kOhBufs = 1;
   static constexpr int oh_off = stages_off + STAGES * stage_bytes;
-  static constexpr int oh_bytes = kOneHot ? 2 * 2 * kXChunk : 0;
+  static constexpr int oh_bytes = kOneHot ? kOhBufs * 2 * kXChunk : 0;
   static constexpr int hist_off = oh_off + oh_bytes;          // per-CTA counts, K <= 128
   static constexpr int hist_bytes = kOneHot ? 128 * 4 : 0;
   static constexpr int merge_off = hist_off + hist_bytes;
@@ -552,7 +557,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   }
   if constexpr (L::kOneHot) {
     // one-hot buffers start all zero (each tile then sets one element per
-    // point and clears the element it set two tiles earlier); counts zero
+    // point and clears the element it set in the buffer's previous use);
+    // counts zero
     uint4* oh = reinterpret_cast<uint4*>(smem + L::oh_off);
     for (int i = threadIdx.x; i < L::oh_bytes / 16; i += blockDim.x) oh[i] = make_uint4(0, 0, 0, 0);
     int* hist = reinterpret_cast<int*>(smem + L::hist_off);
@@ -681,8 +687,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
               return false;
             tc_fence_after();
           }
-          const int par = ohn & 1;
-          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn >> 1) & 1), abort_flag,
+          const int par = ohn % L::kOhBufs;
+          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn / L::kOhBufs) & 1), abort_flag,
                          p.status, FK_DEV_WAIT_TIMEOUT))
             return false;
           tc_fence_after();
@@ -815,6 +821,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     int it = 0;
     bool ok = true;
     int prev_lab[2] = {-1, -1};  // one-hot: the element this point set in each buffer
+    static_assert(L::kOhBufs <= 2, "prev_lab covers two one-hot buffers");
     int fln = 0;                 // one-hot: batch flushes done
     // x_sq of this thread's point in tile t (0 past N), fetched one tile
     // ahead so the tile's first distances do not wait on an HBM read
@@ -998,28 +1005,30 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
         if constexpr (L::kOneHot) {
           // count the point (warp-aggregated shared atomics), then mark it in
-          // this tile's one-hot buffer: clear the element it set two tiles ago,
-          // set (label, point) to 1
+          // this tile's one-hot buffer: clear the element it set in the
+          // buffer's previous use, set (label, point) to 1
           const int lab = valid ? idx : -1;
           const unsigned grp = __match_any_sync(0xffffffffu, lab);
           if (lab >= 0 && lane == __ffs(grp) - 1)
             atomicAdd(reinterpret_cast<int*>(smem + L::hist_off) + lab, __popc(grp));
-          const bool got2 = mbar_wait(&oh_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          const int ob_i = it % L::kOhBufs;
+          const uint32_t oph = static_cast<uint32_t>((it / L::kOhBufs) & 1);
+          const bool got2 = mbar_wait(&oh_empty[ob_i], oph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
           if (!__all_sync(0xffffffffu, got2)) {
             ok = false;
             break;
           }
-          uint8_t* ob = smem + L::oh_off + par * 2 * kXChunk + (row >> 6) * kXChunk;
+          uint8_t* ob = smem + L::oh_off + ob_i * 2 * kXChunk + (row >> 6) * kXChunk;
           const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
           auto elem = [&](int k) -> unsigned short* {
             return reinterpret_cast<unsigned short*>(
                 ob + k * kChunkB + ((((pb >> 4) ^ (k & 7))) << 4) + (pb & 15));
           };
-          if (prev_lab[par] >= 0) *elem(prev_lab[par]) = 0;
+          if (prev_lab[ob_i] >= 0) *elem(prev_lab[ob_i]) = 0;
           if (lab >= 0) *elem(lab) = Pack2<T>::kOne;
-          prev_lab[par] = lab;
+          prev_lab[ob_i] = lab;
           fence_proxy_async_smem();
-          mbar_arrive(&oh_full[par]);
+          mbar_arrive(&oh_full[ob_i]);
         }
         if constexpr (L::kSumWarps && XRES) {
           // hand the label (or -1 past N) to the sum warps
