@@ -75,7 +75,13 @@ constexpr bool split_mode(int mode) { return mode == 2 || mode == 4; }
 template <int MODE, bool XRES, int STAGES, bool FUSE = false, int EPI = 8, int KC = kCent,
           bool RESC = false>
 struct Layout {
-  static constexpr int kGroups = EPI / 4;  // column groups of each centroid tile
+  // Narrow tiles (K <= 128, resident centroids): the two epilogue warpgroups
+  // take alternate point tiles and each thread reduces all 128 columns of its
+  // point, so no column-group merge is needed and a warpgroup has two tile
+  // periods for its tile.  Wide tiles: both warpgroups share every tile, one
+  // column group each, merged through shared memory.
+  static constexpr bool kAlt = RESC && KC < kCent;
+  static constexpr int kGroups = kAlt ? 1 : EPI / 4;  // column groups of each centroid tile
   static constexpr int kSplit = split_mode(MODE) ? 2 : 1;  // hi/lo copies for 3xTF32
   static constexpr int kCChunk = KC * kChunkB;        // one 128-byte column chunk of a tile
   // Fused accumulation comes in two forms: with 256-column tiles (large K)
@@ -110,8 +116,8 @@ struct Layout {
   static constexpr int kOhBufs = 1;
   static constexpr int oh_off = stages_off + STAGES * stage_bytes;
   static constexpr int oh_bytes = kOneHot ? kOhBufs * 2 * kXChunk : 0;
-  static constexpr int hist_off = oh_off + oh_bytes;          // per-CTA counts, K <= 128
-  static constexpr int hist_bytes = kOneHot ? 128 * 4 : 0;
+  static constexpr int hist_off = oh_off + oh_bytes;  // counts per epilogue warpgroup, K <= 128
+  static constexpr int hist_bytes = kOneHot ? 2 * 128 * 4 : 0;
   static constexpr int merge_off = hist_off + hist_bytes;
   // [parity][group 1..G-1][row] (value, index) candidates for the merge
   static constexpr int merge_bytes = 2 * (kGroups - 1) * kRows * 8;
@@ -126,8 +132,8 @@ struct Layout {
   static constexpr int bar_off = save_off + save_bytes;
   // x_full[XB] x_empty[XB] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
-  // oh_full[2] oh_empty[2] sums_full[1] sums_empty[1] fl_ready[1] fl_done[1]
-  static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1 + 8;
+  // oh_full[2] oh_empty[2] sums_full[1] sums_empty[1] wg_bar[2] sums_full_odd[1]
+  static constexpr int nbars = 2 * XB + 3 * STAGES + 2 * kAcc + 4 + 4 + 1 + 9;
   static constexpr int misc_off = bar_off + nbars * 8;
   static constexpr int total = misc_off + 16 + 1024;  // + slack for 1024-byte alignment
   static constexpr bool kExtra = split_mode(MODE) || kSumWarps;  // warpgroup 3
@@ -137,11 +143,12 @@ struct Layout {
   // count before launching.  Control warps shrink to kCtlRegs, the extra
   // warpgroup to kExtraRegs, and the epilogue takes the rest.
   static constexpr int kLaunchRegs = threads == 384 ? 168 : 128;
-  static constexpr int kCtlRegs = kOneHot ? 96 : 72;
+  static constexpr int kCtlRegs = kOneHot ? 88 : 72;
   static constexpr int kExtraRegs = FUSE ? 96 : 72;
   static constexpr int kEpiRegs =
       ((threads * kLaunchRegs - 128 * kCtlRegs - (kExtra ? 128 * kExtraRegs : 0)) / (EPI * 32)) & ~7;
   static_assert(EPI == 8, "two epilogue warpgroups");
+  static_assert(!kOneHot || kAlt, "one-hot accumulation runs with alternating warpgroups");
   static_assert(threads == 384 || threads == 512, "three or four warpgroups");
   static_assert(kEpiRegs <= 256 && kEpiRegs >= kLaunchRegs, "epilogue register budget");
 };
@@ -516,8 +523,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   uint64_t* oh_empty = oh_full + 2;      // its sums MMAs done (buffer and x tile free)
   uint64_t* sums_full = oh_empty + 2;    // a batch's sums complete in TMEM
   uint64_t* sums_empty = sums_full + 1;  // the epilogue has added them to global memory
-  uint64_t* fl_ready = sums_empty + 1;   // epilogue warps done with a batch's last tile
-  uint64_t* fl_done = fl_ready + 1;      // the batch's sums and counts added, counts reset
+  uint64_t* wg_bar = sums_empty + 1;     // [2] barriers of each epilogue warpgroup's 128 threads
+  uint64_t* sums_full_odd = wg_bar + 2;  // sums_full of the CTA's odd batches (one-hot)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
 
@@ -530,13 +537,15 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
     for (int i = 0; i < kAcc; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiWarps * 32);
+      mbar_init(&acc_empty[i], L::kAlt ? 128 : kEpiWarps * 32);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&lab_full[i], 128);
       mbar_init(&lab_empty[i], 128);
-      mbar_init(&merge_full[i], (kGroups - 1) * 128);
-      mbar_init(&merge_empty[i], 128);
+      if (kGroups > 1) {
+        mbar_init(&merge_full[i], (kGroups - 1) * 128);
+        mbar_init(&merge_empty[i], 128);
+      }
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&c_full[s], 1);
@@ -549,9 +558,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       mbar_init(&oh_empty[i], 1);
     }
     mbar_init(sums_full, 1);
-    mbar_init(sums_empty, kEpiWarps * 32);
-    mbar_init(fl_ready, kEpiWarps * 32);
-    mbar_init(fl_done, kEpiWarps * 32);
+    mbar_init(sums_full_odd, 1);
+    // one warpgroup reads a batch's sums (one-hot form)
+    mbar_init(sums_empty, 128);
+    mbar_init(&wg_bar[0], 128);
+    mbar_init(&wg_bar[1], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     uint4* oh = reinterpret_cast<uint4*>(smem + L::oh_off);
     for (int i = threadIdx.x; i < L::oh_bytes / 16; i += blockDim.x) oh[i] = make_uint4(0, 0, 0, 0);
     int* hist = reinterpret_cast<int*>(smem + L::hist_off);
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) hist[i] = 0;
+    for (int i = threadIdx.x; i < L::hist_bytes / 4; i += blockDim.x) hist[i] = 0;
     fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -673,8 +684,9 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       // sums[k][d] += sum_p onehot[k][p] * x[p][d] into the TMEM sums columns,
       // A = one-hot (K-major: points contiguous per centroid), B = the tile's
       // x buffer read MN-major (dims contiguous per point; LBO = the 64-dim
-      // chunk stride, SBO = 8 points).  A batch's last tile commits sums_full;
-      // the next batch's first sums MMA waits until the epilogue has read them.
+      // chunk stride, SBO = 8 points).  A batch's last tile commits sums_full
+      // (sums_full_odd for the CTA's odd batches); the next batch's first sums
+      // MMA waits until the epilogue has read them (sums_empty).
       int pt = -1, pxb = 0;       // tile whose sums MMAs are pending, its x buffer
       int ohn = 0, fln = 0;       // one-hot buffers consumed, flushes done
       bool sums_on = false;       // the current batch's sums already started
@@ -705,7 +717,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           mma_commit(&x_empty[xbuf]);
           ++ohn;
           if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
-            mma_commit(sums_full);
+            mma_commit((fln & 1) ? sums_full_odd : sums_full);
             ++fln;
             sums_on = false;
           }
@@ -813,16 +825,18 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     setmaxnreg_inc<L::kEpiRegs>();
     const int ew = warp - kEpiWarp0;
     const int q = warp & 3;          // TMEM lane quarter this warp may access
-    const int h = ew >> 2;           // column group: kGCols columns of each tile
+    const int wg = ew >> 2;          // epilogue warpgroup
+    const int h = L::kAlt ? 0 : wg;  // column group: kGCols columns of each tile
     const int row = q * 32 + lane;   // point within the tile
     uint2* merge = reinterpret_cast<uint2*>(smem + L::merge_off);
-    int ab = 0;
-    uint32_t aph = 0;
-    int it = 0;
+    // alternating warpgroups: warpgroup wg takes the CTA's tiles wg, wg+2, ...
+    constexpr int kStep = L::kAlt ? 2 : 1;
+    const int it0 = L::kAlt ? wg : 0;
+    int ab = it0 % kAcc;
+    uint32_t aph = static_cast<uint32_t>((it0 / kAcc) & 1);
+    int it = it0;                    // tile index within the CTA's range
     bool ok = true;
-    int prev_lab[2] = {-1, -1};  // one-hot: the element this point set in each buffer
-    static_assert(L::kOhBufs <= 2, "prev_lab covers two one-hot buffers");
-    int fln = 0;                 // one-hot: batch flushes done
+    int wsn = 0;                     // alternating: uses of this warpgroup's barrier
     // x_sq of this thread's point in tile t (0 past N), fetched one tile
     // ahead so the tile's first distances do not wait on an HBM read
     auto load_xsq = [&](int t) -> float {
@@ -830,13 +844,26 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       return (n < p.N && p.xsq) ? load_f(p.xsq, (t / p.ntn) * p.sxq_b + n * p.sxq_n, p.xsq_dtype)
                                 : 0.0f;
     };
-    float xsq_next = t_begin < t_end ? load_xsq(t_begin) : 0.0f;
-    for (int t = t_begin; ok && t < t_end; ++t, ++it) {
+    // bounded barrier of this warpgroup's 128 threads (alternating form)
+    auto wg_sync = [&]() -> bool {
+      uint64_t* bar = &wg_bar[wg];
+      mbar_arrive(bar);
+      const bool got = mbar_wait(bar, static_cast<uint32_t>(wsn & 1), abort_flag, p.status,
+                                 FK_DEV_WAIT_TIMEOUT);
+      ++wsn;
+      return __all_sync(0xffffffffu, got);
+    };
+    float xsq_next = t_begin + it0 < t_end ? load_xsq(t_begin + it0) : 0.0f;
+    for (int t = t_begin + it0; ok && t < t_end; t += kStep, it += kStep) {
       const int b = t / p.ntn;
       const int n = (t % p.ntn) * kRows + row;
       const bool valid = n < p.N;
       const float xsq_f = xsq_next;
-      if (t + 1 < t_end) xsq_next = load_xsq(t + 1);
+      if (t + kStep < t_end) xsq_next = load_xsq(t + kStep);
+      if constexpr (L::kAlt) {   // one accumulator per tile, used in tile order
+        ab = it % kAcc;
+        aph = static_cast<uint32_t>((it / kAcc) & 1);
+      }
 
       using Argmin = typename std::conditional<
           MODE == 0, ArgminSaved<T>,
@@ -970,65 +997,80 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       else
         am.result(val, idx);
 
-      // Merge the column groups: groups 1.. publish, group 0 decides.
+      // Merge the column groups (wide tiles): groups 1.. publish, group 0 decides.
       const int par = it & 1;
       const uint32_t mph = static_cast<uint32_t>((it >> 1) & 1);
-      uint2* mslots = merge + par * (kGroups - 1) * kRows;
-      if (h != 0) {
-        const bool got = mbar_wait(&merge_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-        mslots[(h - 1) * kRows + row] = make_uint2(__float_as_uint(val), static_cast<uint32_t>(idx));
-        mbar_arrive(&merge_full[par]);
-      } else {
-        const bool got = mbar_wait(&merge_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int gg = 1; gg < kGroups; ++gg) {
-          const uint2 o = mslots[(gg - 1) * kRows + row];
-          const float vo = __uint_as_float(o.x);
-          const int io = static_cast<int>(o.y);
-          if (argmin_better(vo, io, val, idx)) {
-            val = vo;
-            idx = io;
+      bool decide = true;
+      if constexpr (kGroups > 1) {
+        uint2* mslots = merge + par * (kGroups - 1) * kRows;
+        if (h != 0) {
+          const bool got = mbar_wait(&merge_empty[par], mph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
           }
+          mslots[(h - 1) * kRows + row] = make_uint2(__float_as_uint(val), static_cast<uint32_t>(idx));
+          mbar_arrive(&merge_full[par]);
+          decide = false;
+        } else {
+          const bool got = mbar_wait(&merge_full[par], mph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int gg = 1; gg < kGroups; ++gg) {
+            const uint2 o = mslots[(gg - 1) * kRows + row];
+            const float vo = __uint_as_float(o.x);
+            const int io = static_cast<int>(o.y);
+            if (argmin_better(vo, io, val, idx)) {
+              val = vo;
+              idx = io;
+            }
+          }
+          mbar_arrive(&merge_empty[par]);
         }
-        mbar_arrive(&merge_empty[par]);
+      }
+      if (decide) {
         if (valid) {
           p.out[b * p.so_b + static_cast<int64_t>(n) * p.so_n] = idx;
           if (p.counts && !L::kOneHot) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + idx, 1);
         }
         if constexpr (L::kOneHot) {
-          // count the point (warp-aggregated shared atomics), then mark it in
-          // this tile's one-hot buffer: clear the element it set in the
-          // buffer's previous use, set (label, point) to 1
+          // Count the point in this warpgroup's shared counts (warp-aggregated
+          // atomics), then write the warp's 32 columns of the tile's one-hot
+          // operand once the sums MMAs of the previous tile are done with it.
+          // The warp rewrites its points' whole columns (zeros, then 1 at
+          // (label, point)), so nothing of the previous tile survives, whichever
+          // warpgroup wrote it.  Lane -> 16-byte unit u (8 points) and rows
+          // 8i + c: every 8 consecutive lanes cover the eight 16-byte positions
+          // of the swizzled 128-byte rows (conflict-free stores).
           const int lab = valid ? idx : -1;
+          int* hist = reinterpret_cast<int*>(smem + L::hist_off) + wg * 128;
           const unsigned grp = __match_any_sync(0xffffffffu, lab);
-          if (lab >= 0 && lane == __ffs(grp) - 1)
-            atomicAdd(reinterpret_cast<int*>(smem + L::hist_off) + lab, __popc(grp));
-          const int ob_i = it % L::kOhBufs;
-          const uint32_t oph = static_cast<uint32_t>((it / L::kOhBufs) & 1);
-          const bool got2 = mbar_wait(&oh_empty[ob_i], oph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          if (lab >= 0 && lane == __ffs(grp) - 1) atomicAdd(hist + lab, __popc(grp));
+          const uint32_t oph = static_cast<uint32_t>(it & 1);
+          const bool got2 = mbar_wait(&oh_empty[0], oph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
           if (!__all_sync(0xffffffffu, got2)) {
             ok = false;
             break;
           }
-          uint8_t* ob = smem + L::oh_off + ob_i * 2 * kXChunk + (row >> 6) * kXChunk;
-          const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
-          auto elem = [&](int k) -> unsigned short* {
-            return reinterpret_cast<unsigned short*>(
-                ob + k * kChunkB + ((((pb >> 4) ^ (k & 7))) << 4) + (pb & 15));
-          };
-          if (prev_lab[ob_i] >= 0) *elem(prev_lab[ob_i]) = 0;
-          if (lab >= 0) *elem(lab) = Pack2<T>::kOne;
-          prev_lab[ob_i] = lab;
+          uint8_t* ob = smem + L::oh_off + (row >> 6) * kXChunk;  // the warp's 64-point chunk
+          const int u = 4 * (q & 1) + (lane & 3);
+          const int c = (((lane >> 2) & 1) << 2) | (lane >> 3);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k = 8 * i + c;
+            *reinterpret_cast<uint4*>(ob + k * kChunkB + ((u ^ (k & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          }
+          __syncwarp();
+          if (lab >= 0) {
+            const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
+            *reinterpret_cast<unsigned short*>(ob + lab * kChunkB + (((pb >> 4) ^ (lab & 7)) << 4) +
+                                               (pb & 15)) = Pack2<T>::kOne;
+          }
           fence_proxy_async_smem();
-          mbar_arrive(&oh_full[ob_i]);
+          mbar_arrive(&oh_full[0]);
         }
         if constexpr (L::kSumWarps && XRES) {
           // hand the label (or -1 past N) to the sum warps
@@ -1042,51 +1084,63 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
       }
       if constexpr (L::kOneHot) {
-        // a batch's last tile in this CTA: add the TMEM sums (lanes = centroids,
-        // this warp's 64 of the 128 dimension columns) and the shared counts to
-        // the global accumulators, reset the counts
+        // This warpgroup's last tile of the batch: add its shared counts to
+        // the global counts and reset them (a barrier of the warpgroup on
+        // each side: every count added before, none of the next batch's
+        // before the reset).
+        if (t + kStep >= t_end || (t + kStep) / p.ntn != b) {
+          if (!wg_sync()) {
+            ok = false;
+            break;
+          }
+          int* hist = reinterpret_cast<int*>(smem + L::hist_off) + wg * 128;
+          const int cnt = hist[row];
+          if (cnt && p.counts && row < p.K)
+            atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + row, cnt);
+          hist[row] = 0;
+          if (!wg_sync()) {
+            ok = false;
+            break;
+          }
+        }
+        // The batch's last tile: add the TMEM sums (lanes = centroids, 128
+        // dimension columns) to the global sums.  Batches alternate between
+        // two sums_full barriers (batch j of the CTA: barrier j & 1, phase
+        // (j >> 1) & 1), so a warpgroup that never saw the previous batch's
+        // completion cannot mistake it for this one's.
         if (t + 1 == t_end || (t + 1) / p.ntn != b) {
-          const uint32_t fph = static_cast<uint32_t>(fln & 1);
-          mbar_arrive(fl_ready);
-          bool got3 = mbar_wait(fl_ready, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-          got3 = got3 && mbar_wait(sums_full, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          const int j = b - t_begin / p.ntn;
+          uint64_t* sf = (j & 1) ? sums_full_odd : sums_full;
+          const bool got3 =
+              mbar_wait(sf, static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
           if (!__all_sync(0xffffffffu, got3)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t sa[32], sb[32];
           const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                              static_cast<uint32_t>(L::kSumsCol + h * 64);
-          tmem_ld32(ta, sa);
-          tmem_ld32(ta + 32, sb);
-          tmem_ld_wait(sa);
-          tmem_ld_wait(sb);
-          tc_fence_before();
-          mbar_arrive(sums_empty);
-          const int k = q * 32 + lane;   // this thread's centroid
-          if (k < p.K) {
-            float* dst = p.sums + (static_cast<int64_t>(b) * p.K + k) * p.D;
-            const int d0 = h * 64;
+                              static_cast<uint32_t>(L::kSumsCol);
+          float* dst = p.sums + (static_cast<int64_t>(b) * p.K + row) * p.D;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (d0 + j < p.D) atomicAdd(dst + d0 + j, __uint_as_float(sa[j]));
-              if (d0 + 32 + j < p.D) atomicAdd(dst + d0 + 32 + j, __uint_as_float(sb[j]));
+          for (int half = 0; half < 2; ++half) {
+            uint32_t sa[32], sb[32];
+            tmem_ld32(ta + half * 64, sa);
+            tmem_ld32(ta + half * 64 + 32, sb);
+            tmem_ld_wait(sa);
+            tmem_ld_wait(sb);
+            if (half == 1) {
+              tc_fence_before();
+              mbar_arrive(sums_empty);
             }
-            if (h == 0) {
-              int* hist = reinterpret_cast<int*>(smem + L::hist_off);
-              const int c = hist[k];
-              if (c) atomicAdd(p.counts + static_cast<int64_t>(b) * p.K + k, c);
-              hist[k] = 0;
+            if (row < p.K) {
+              const int d0 = half * 64;
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                if (d0 + jj < p.D) atomicAdd(dst + d0 + jj, __uint_as_float(sa[jj]));
+                if (d0 + 32 + jj < p.D) atomicAdd(dst + d0 + 32 + jj, __uint_as_float(sb[jj]));
+              }
             }
           }
-          mbar_arrive(fl_done);
-          const bool got4 = mbar_wait(fl_done, fph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-          if (!__all_sync(0xffffffffu, got4)) {
-            ok = false;
-            break;
-          }
-          ++fln;
         }
       }
     }

@@ -253,7 +253,10 @@ def test_accumulate_privatised_and_sorted_paths(fk, dt, B, N, K, D, idt):
     # CTA ranges that cross many batch boundaries, one long batch with K = 128, K = 1,
     # and float32 x_sq (mode 1)
     ("float16", 64, 1000, 100, 128), ("bfloat16", 40, 700, 17, 64),
-    ("float16", 1, 300000, 128, 128), ("float16", 3, 129, 1, 8), ("float16-xsq32", 5, 3000, 60, 128)])
+    ("float16", 1, 300000, 128, 128), ("float16", 3, 129, 1, 8), ("float16-xsq32", 5, 3000, 60, 128),
+    # one-hot form: every tile its own batch (each CTA flushes after every tile, both
+    # epilogue warpgroups and both sums barriers), and three tiles per batch
+    ("float16", 300, 100, 64, 128), ("bfloat16", 37, 260, 128, 96)])
 def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     """fk_assign_accumulate (fused for 16-bit D<=128: one-hot tensor-core sums for K<=128,
     sum warps for larger K; privatised or sorted otherwise) equals fk_assign + torch

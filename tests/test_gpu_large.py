@@ -71,7 +71,9 @@ def _batched_case(B=3, N=90_000, D=20, K=24, seed=9):
 def test_kmeans_largeN_batched_equals_per_batch(fk, dtype, resident):
     """Batched x (B, N, D) runs the B problems independently: one pass from the
     same centroids gives each batch's labels bit for bit and its centroids to
-    float rounding.  D=20 exercises padded rows; float16 the on-device
+    float rounding: the float32 sums add in another order (other CTA ranges,
+    atomics), so a stored float16 centroid may differ by one rounding step
+    (2^-10 relative).  D=20 exercises padded rows; float16 the on-device
     conversion of streamed float32 blocks."""
     x, c0 = _batched_case()
     B, N, D = x.shape
@@ -86,7 +88,8 @@ def test_kmeans_largeN_batched_equals_per_batch(fk, dtype, resident):
                                   init_centroids=torch.from_numpy(c0[b]), device="cuda:0",
                                   dtype=dtype, resident=resident)
         assert torch.equal(lab[b], lb)
-        assert_centroids(_np(cent[b])[None], _np(cb)[None], f"batch {b}", rtol=1e-5)
+        assert_centroids(_np(cent[b])[None], _np(cb)[None], f"batch {b}",
+                         rtol=1e-5 if dtype == torch.float32 else 2.0 ** -10)
     # against the oracle (one teacher-forced pass)
     dt = "float32" if dtype == torch.float32 else "float16"
     xq = ko.round_to(x, dt)
