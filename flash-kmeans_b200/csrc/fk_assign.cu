@@ -90,8 +90,11 @@ struct Layout {
   // matrix times the tile's x into a TMEM sums accumulator (kOneHot).
   static constexpr bool kOneHot = FUSE && KC < kCent;
   static constexpr bool kSumWarps = FUSE && !kOneHot;
-  // TMEM accumulators (the one-hot form keeps 128 columns for the sums)
-  static constexpr int kAcc = kOneHot ? (kTmemCols - 128) / KC : kTmemCols / KC;
+  // TMEM accumulators.  The one-hot form keeps 128 columns for the sums and
+  // uses two accumulators, so with alternating warpgroups each accumulator
+  // (and its barriers) belongs to one warpgroup: a warpgroup only waits for
+  // phases whose predecessor it observed itself.
+  static constexpr int kAcc = kOneHot ? 2 : kTmemCols / KC;
   static constexpr int kSumsCol = kAcc * KC;            // first TMEM column of the sums
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
   // or (narrow tiles, one centroid tile per point tile) lets x loads run
@@ -99,7 +102,11 @@ struct Layout {
   // (RESC) the ring is small and five x tiles fit (four next to the one-hot
   // buffer: a one-hot tile holds its x buffer until its sums MMAs finish, so
   // the ring must cover the load latency plus two epilogue periods)
-  static constexpr int XB = RESC ? (kOneHot ? 4 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
+  // mode 0 keeps its saved chunk in registers in the one-hot form; the other
+  // modes 0, 3 and 4 use shared-memory slots
+  static constexpr bool kRegSave = kOneHot && MODE == 0;
+  static constexpr bool kSmemSave = (MODE == 0 && !kRegSave) || MODE >= 3;
+  static constexpr int XB = RESC ? ((kOneHot && kSmemSave) ? 4 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -128,7 +135,7 @@ struct Layout {
   // (conflict-free stores)
   static constexpr int save_stride = EPI * 32;  // in 16-byte units
   static constexpr int save_off = lab_off + lab_bytes;
-  static constexpr int save_bytes = (MODE == 0 || MODE >= 3) ? 4 * save_stride * 16 : 0;
+  static constexpr int save_bytes = kSmemSave ? 4 * save_stride * 16 : 0;
   static constexpr int bar_off = save_off + save_bytes;
   // x_full[XB] x_empty[XB] c_full[S] c_empty[S] conv_full[S] acc_full[A] acc_empty[A]
   // merge_full[2] merge_empty[2] lab_full[2] lab_empty[2] final[1]
@@ -143,12 +150,13 @@ struct Layout {
   // count before launching.  Control warps shrink to kCtlRegs, the extra
   // warpgroup to kExtraRegs, and the epilogue takes the rest.
   static constexpr int kLaunchRegs = threads == 384 ? 168 : 128;
-  static constexpr int kCtlRegs = kOneHot ? 88 : 72;
+  static constexpr int kCtlRegs = 72;
   static constexpr int kExtraRegs = FUSE ? 96 : 72;
   static constexpr int kEpiRegs =
       ((threads * kLaunchRegs - 128 * kCtlRegs - (kExtra ? 128 * kExtraRegs : 0)) / (EPI * 32)) & ~7;
   static_assert(EPI == 8, "two epilogue warpgroups");
   static_assert(!kOneHot || kAlt, "one-hot accumulation runs with alternating warpgroups");
+  static_assert(!kAlt || kAcc % 2 == 0, "alternating warpgroups need an even accumulator ring");
   static_assert(threads == 384 || threads == 512, "three or four warpgroups");
   static_assert(kEpiRegs <= 256 && kEpiRegs >= kLaunchRegs, "epilogue register budget");
 };
@@ -210,6 +218,17 @@ struct Pack2;
     uint32_t r;                                                                                  \
     asm("min.NaN." SFX " %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));                               \
     return r;                                                                                    \
+  }                                                                                              \
+  /* a strict improvement of the chunk minimum mm over best2, or its first NaN         */        \
+  __device__ __forceinline__ static bool improves(uint32_t best2, uint32_t mm) {                 \
+    uint32_t r;                                                                                  \
+    asm("{\n\t.reg .pred p, q, n;\n\t"                                                           \
+        "setp.nan." SFX " n|q, %1, %1;\n\t"                                                      \
+        "setp.ltu.and." SFX " p|q, %2, %1, !n;\n\t"                                              \
+        "selp.u32 %0, 1, 0, p;\n\t}"                                                            \
+        : "=r"(r)                                                                                \
+        : "r"(best2), "r"(mm));                                                                  \
+    return r != 0;                                                                               \
   }                                                                                              \
   /* on a strict improvement of the chunk minimum mm over best2 (or the first NaN),    */        \
   /* store the chunk's 16 packed distances as four 16-byte units `STRIDE` bytes apart  */        \
@@ -342,6 +361,69 @@ struct ArgminSaved {
                    : "=r"(w[4 * u]), "=r"(w[4 * u + 1]), "=r"(w[4 * u + 2]), "=r"(w[4 * u + 3])
                    : "r"(saddr + u * STRIDE)
                    : "memory");
+    int pos = 31;
+    if (val != val) {  // the first NaN of the saved chunk
+#pragma unroll
+      for (int pp = 15; pp >= 0; --pp) {
+        const float h = Pack2<T>::hi(w[pp]), l = Pack2<T>::lo(w[pp]);
+        if (h != h) pos = 2 * pp + 1;
+        if (l != l) pos = 2 * pp;
+      }
+    } else {
+#pragma unroll
+      for (int pp = 15; pp >= 0; --pp) {
+        if (Pack2<T>::hi(w[pp]) == val) pos = 2 * pp + 1;
+        if (Pack2<T>::lo(w[pp]) == val) pos = 2 * pp;
+      }
+    }
+    idx = chunk * 32 + pos;
+  }
+};
+
+// Mode 0 with the saved chunk in registers (narrow one-hot tiles, where the
+// shared-memory slots would cost an x tile buffer): the same rule as
+// ArgminSaved, the winning chunk's 16 packed distances copied to w[] on each
+// strict improvement instead of stored.
+template <typename T>
+struct ArgminRegs {
+  uint32_t best2;
+  int chunk;
+  uint32_t w[16];
+  __device__ __forceinline__ void init(uint32_t) {
+    best2 = Pack2<T>::kInf2;
+    chunk = -1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = 0u;
+  }
+  template <int STRIDE>
+  __device__ __forceinline__ void chunk32(const uint32_t (&v)[32], const uint4 (&cq)[4],
+                                          uint32_t xsq2, int col0) {
+    const uint32_t* cw = reinterpret_cast<const uint32_t*>(cq);
+    uint32_t d[16];
+#pragma unroll
+    for (int pp = 0; pp < 16; ++pp)
+      d[pp] = Pack2<T>::dist(__uint_as_float(v[2 * pp]), __uint_as_float(v[2 * pp + 1]), xsq2, cw[pp]);
+    uint32_t m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = Pack2<T>::min2(d[i], d[i + 8]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = Pack2<T>::min2(m[i], m[i + 4]);
+    m[0] = Pack2<T>::min2(m[0], m[2]);
+    m[1] = Pack2<T>::min2(m[1], m[3]);
+    m[0] = Pack2<T>::min2(m[0], m[1]);
+    const uint32_t mm = Pack2<T>::min2(m[0], __byte_perm(m[0], 0, 0x1032));  // both halves
+    const bool p = Pack2<T>::improves(best2, mm);
+    best2 = p ? mm : best2;
+    chunk = p ? (col0 >> 5) : chunk;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = p ? d[i] : w[i];
+  }
+  template <int STRIDE>
+  __device__ __forceinline__ void result(float& val, int& idx, int first_col) const {
+    val = __int_as_float(0x7f800000);
+    idx = first_col;
+    if (chunk < 0) return;
+    val = Pack2<T>::lo(best2);
     int pos = 31;
     if (val != val) {  // the first NaN of the saved chunk
 #pragma unroll
@@ -520,7 +602,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   uint64_t* lab_empty = lab_full + 2;
   uint64_t* final_bar = lab_empty + 2;
   uint64_t* oh_full = final_bar + 1;     // one-hot operand of a tile written (128 points)
-  uint64_t* oh_empty = oh_full + 2;      // its sums MMAs done (buffer and x tile free)
+  uint64_t* oh_empty = oh_full + 2;      // [tile & 1] its sums MMAs done (buffer and x tile free)
   uint64_t* sums_full = oh_empty + 2;    // a batch's sums complete in TMEM
   uint64_t* sums_empty = sums_full + 1;  // the epilogue has added them to global memory
   uint64_t* wg_bar = sums_empty + 1;     // [2] barriers of each epilogue warpgroup's 128 threads
@@ -679,8 +761,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       uint32_t aph = 0;
       int bi = -1, prev_b = -1;  // RESC: as in the producer
       bool ok = true;
-      // One-hot accumulation: the sums MMAs of tile t run after the assignment
-      // MMAs of tile t+1 (the epilogue needs the labels of t first):
+      // One-hot accumulation: the sums MMAs of tile t run once the epilogue
+      // has written the labels of t as a one-hot operand:
       // sums[k][d] += sum_p onehot[k][p] * x[p][d] into the TMEM sums columns,
       // A = one-hot (K-major: points contiguous per centroid), B = the tile's
       // x buffer read MN-major (dims contiguous per point; LBO = the 64-dim
@@ -713,7 +795,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                     smem_desc_sw128_mn(b0 + s * 16 * kChunkB, kXChunk, 1024), idesc_s,
                     (sums_on || s > 0) ? 1u : 0u);
           sums_on = true;
-          mma_commit(&oh_empty[par]);
+          mma_commit(&oh_empty[ohn & 1]);
           mma_commit(&x_empty[xbuf]);
           ++ohn;
           if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
@@ -724,6 +806,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
         return true;
       };
+      if constexpr (!L::kOneHot) {
       for (int t = t_begin; ok && t < t_end; ++t) {
         bool new_batch = false, last_of_batch = false;
         if constexpr (RESC) {
@@ -810,8 +893,83 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           }
         }
       }
-      if constexpr (L::kOneHot) {
-        if (ok && pt >= 0) ok = sums_mma(pt, pxb);
+      } else {
+        // One-hot form (K <= 128: one centroid tile, resident): the thread
+        // polls both queues and issues whatever is ready - a tile's
+        // assignment MMAs as soon as its x tile and an accumulator are free
+        // (up to kAcc tiles ahead of the epilogue), the sums MMAs of the
+        // oldest labelled tile as soon as its one-hot operand is written - so
+        // the next assignment never waits behind a one-hot tile.
+        int td = t_begin;     // next tile for the assignment MMAs (x buffer xb)
+        int ts = t_begin;     // next tile for the sums MMAs
+        int xs = 0;           // x buffer of tile ts
+        uint64_t idle0 = 0;   // when polling started to make no progress
+        while (ok && ts < t_end) {
+          bool prog = false;
+          if (td < t_end && mbar_test_wait(&x_full[xb], xph) &&
+              mbar_test_wait(&acc_empty[ab], aph ^ 1)) {
+            tc_fence_after();
+            const int b = td / p.ntn;
+            const bool new_batch = b != prev_b;
+            if (new_batch) {
+              ++bi;
+              prev_b = b;
+            }
+            const bool last_of_batch = td + 1 == t_end || (td + 1) / p.ntn != b;
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
+            for (int dc = 0; dc < p.nd; ++dc) {
+              if (new_batch && !mbar_wait(&c_full[dc], static_cast<uint32_t>(bi & 1), abort_flag,
+                                          p.status, FK_DEV_WAIT_TIMEOUT)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t a_addr =
+                  smem_u32(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk);
+              const uint32_t b_addr = smem_u32(smem + L::stages_off + dc * L::stage_bytes + L::st_c);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t off = static_cast<uint32_t>(ks * 32);
+                mma_f16(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off), idesc,
+                        (dc > 0 || ks > 0) ? 1u : 0u);
+              }
+              if (last_of_batch) mma_commit(&c_empty[dc]);
+            }
+            if (!ok) break;
+            mma_commit(&acc_full[ab]);
+            if (++ab == kAcc) { ab = 0; aph ^= 1; }
+            if (++xb == L::XB) { xb = 0; xph ^= 1; }
+            ++td;
+            prog = true;
+          }
+          if (ts < td && mbar_test_wait(&oh_full[0], static_cast<uint32_t>(ohn & 1))) {
+            if (!sums_mma(ts, xs)) {
+              ok = false;
+              break;
+            }
+            if (++xs == L::XB) xs = 0;
+            ++ts;
+            prog = true;
+          }
+          if (prog) {
+            idle0 = 0;
+            continue;
+          }
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          const uint64_t now = globaltimer_ns();
+          if (idle0 == 0) {
+            idle0 = now;
+          } else if (now - idle0 > FK_WAIT_LIMIT_NS) {
+            *abort_flag = FK_DEV_WAIT_TIMEOUT;
+            if (p.status) atomicCAS(p.status, 0, FK_DEV_WAIT_TIMEOUT);
+            ok = false;
+            break;
+          }
+          __nanosleep(20);
+        }
       }
       // All MMAs this thread issued must finish before TMEM is released.
       mma_commit(final_bar);
@@ -866,7 +1024,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       }
 
       using Argmin = typename std::conditional<
-          MODE == 0, ArgminSaved<T>,
+          MODE == 0,
+          typename std::conditional<L::kRegSave, ArgminRegs<T>, ArgminSaved<T>>::type,
           typename std::conditional<(MODE >= 3), ArgmaxSaved, ArgminF32<T, MODE>>::type>::type;
       constexpr int kSaveStride = L::save_stride * 16;  // bytes between a slot's 16-byte units
       Argmin am;
@@ -1049,11 +1208,17 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           int* hist = reinterpret_cast<int*>(smem + L::hist_off) + wg * 128;
           const unsigned grp = __match_any_sync(0xffffffffu, lab);
           if (lab >= 0 && lane == __ffs(grp) - 1) atomicAdd(hist + lab, __popc(grp));
-          const uint32_t oph = static_cast<uint32_t>(it & 1);
-          const bool got2 = mbar_wait(&oh_empty[0], oph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
-          if (!__all_sync(0xffffffffu, got2)) {
-            ok = false;
-            break;
+          // tile u's sums MMAs arrive on oh_empty[u & 1]: waiting for tile
+          // it-1 (the other warpgroup's) on its own barrier is at most one
+          // phase ahead, since this warpgroup saw tile it-3 consumed before
+          // writing tile it-2
+          if (it > 0) {
+            const bool got2 = mbar_wait(&oh_empty[(it - 1) & 1], static_cast<uint32_t>(((it - 1) >> 1) & 1),
+                                        abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+            if (!__all_sync(0xffffffffu, got2)) {
+              ok = false;
+              break;
+            }
           }
           uint8_t* ob = smem + L::oh_off + (row >> 6) * kXChunk;  // the warp's 64-point chunk
           const int u = 4 * (q & 1) + (lane & 3);
