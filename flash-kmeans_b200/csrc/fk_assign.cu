@@ -106,7 +106,7 @@ struct Layout {
   // modes 0, 3 and 4 use shared-memory slots
   static constexpr bool kRegSave = kOneHot && MODE == 0;
   static constexpr bool kSmemSave = (MODE == 0 && !kRegSave) || MODE >= 3;
-  static constexpr int XB = RESC ? ((kOneHot && kSmemSave) ? 4 : 5) : ((FUSE || KC < kCent) ? 3 : 2);
+  static constexpr int XB = RESC ? (kOneHot ? (kSmemSave ? 3 : 4) : 5) : ((FUSE || KC < kCent) ? 3 : 2);
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
@@ -115,12 +115,12 @@ struct Layout {
   static constexpr int st_xlo = st_x + kXChunk;           // x chunk lo (mode 2)
   static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
-  // one-hot operand [point chunk 0..1][centroid row][64 points], 16-bit,
-  // 128-byte swizzle (K-major A operand of the sums MMA).  One buffer: the
-  // epilogue of tile t writes it after the sums MMAs of tile t-1 (issued right
-  // after the assignment MMAs of tile t) have finished, by which time it has
-  // reduced the whole tile.
-  static constexpr int kOhBufs = 1;
+  // one-hot operands [warpgroup][point chunk 0..1][centroid row][64 points],
+  // 16-bit, 128-byte swizzle (K-major A operand of the sums MMA).  One buffer
+  // per epilogue warpgroup: a warpgroup rewrites its buffer once the sums MMAs
+  // of its previous tile (two tiles back) are done, so the two warpgroups do
+  // not wait on each other's sums.
+  static constexpr int kOhBufs = 2;
   static constexpr int oh_off = stages_off + STAGES * stage_bytes;
   static constexpr int oh_bytes = kOneHot ? kOhBufs * 2 * kXChunk : 0;
   static constexpr int hist_off = oh_off + oh_bytes;  // counts per epilogue warpgroup, K <= 128
@@ -148,9 +148,10 @@ struct Layout {
   // Register budgets (setmaxnreg).  kLaunchRegs is what ptxas gives a thread
   // under __launch_bounds__(threads, 1); the host checks the kernel's actual
   // count before launching.  Control warps shrink to kCtlRegs, the extra
-  // warpgroup to kExtraRegs, and the epilogue takes the rest.
+  // warpgroup to kExtraRegs, and the epilogue takes the rest (the budgets
+  // are the smallest at which ptxas reports no spills for each instance).
   static constexpr int kLaunchRegs = threads == 384 ? 168 : 128;
-  static constexpr int kCtlRegs = 72;
+  static constexpr int kCtlRegs = (kAlt && MODE != 0) ? 80 : 72;
   static constexpr int kExtraRegs = FUSE ? 96 : 72;
   static constexpr int kEpiRegs =
       ((threads * kLaunchRegs - 128 * kCtlRegs - (kExtra ? 128 * kExtraRegs : 0)) / (EPI * 32)) & ~7;
@@ -602,7 +603,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
   uint64_t* lab_empty = lab_full + 2;
   uint64_t* final_bar = lab_empty + 2;
   uint64_t* oh_full = final_bar + 1;     // one-hot operand of a tile written (128 points)
-  uint64_t* oh_empty = oh_full + 2;      // [tile & 1] its sums MMAs done (buffer and x tile free)
+  uint64_t* oh_empty = oh_full + 2;      // its sums MMAs done (buffer and x tile free)
   uint64_t* sums_full = oh_empty + 2;    // a batch's sums complete in TMEM
   uint64_t* sums_empty = sums_full + 1;  // the epilogue has added them to global memory
   uint64_t* wg_bar = sums_empty + 1;     // [2] barriers of each epilogue warpgroup's 128 threads
@@ -619,7 +620,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
     for (int i = 0; i < kAcc; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], L::kAlt ? 128 : kEpiWarps * 32);
+      mbar_init(&acc_empty[i], L::kAlt ? 4 : kEpiWarps * 32);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&lab_full[i], 128);
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
     mbar_init(final_bar, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&oh_full[i], 128);
+      mbar_init(&oh_full[i], 4);
       mbar_init(&oh_empty[i], 1);
     }
     mbar_init(sums_full, 1);
@@ -781,8 +782,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
               return false;
             tc_fence_after();
           }
-          const int par = ohn % L::kOhBufs;
-          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn / L::kOhBufs) & 1), abort_flag,
+          const int par = ohn & 1;   // tile ohn of the CTA: its warpgroup's buffer
+          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn >> 1) & 1), abort_flag,
                          p.status, FK_DEV_WAIT_TIMEOUT))
             return false;
           tc_fence_after();
@@ -795,7 +796,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                     smem_desc_sw128_mn(b0 + s * 16 * kChunkB, kXChunk, 1024), idesc_s,
                     (sums_on || s > 0) ? 1u : 0u);
           sums_on = true;
-          mma_commit(&oh_empty[ohn & 1]);
+          mma_commit(&oh_empty[par]);
           mma_commit(&x_empty[xbuf]);
           ++ohn;
           if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
@@ -942,7 +943,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
             ++td;
             prog = true;
           }
-          if (ts < td && mbar_test_wait(&oh_full[0], static_cast<uint32_t>(ohn & 1))) {
+          if (ts < td && mbar_test_wait(&oh_full[ohn & 1], static_cast<uint32_t>((ohn >> 1) & 1))) {
             if (!sums_mma(ts, xs)) {
               ok = false;
               break;
@@ -995,6 +996,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     int it = it0;                    // tile index within the CTA's range
     bool ok = true;
     int wsn = 0;                     // alternating: uses of this warpgroup's barrier
+    int prev_lab = -1;               // one-hot: the element this thread set in its buffer
     // x_sq of this thread's point in tile t (0 past N), fetched one tile
     // ahead so the tile's first distances do not wait on an HBM read
     auto load_xsq = [&](int t) -> float {
@@ -1047,9 +1049,16 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         tc_fence_after();
         return true;
       };
+      // (alternating form: one arrival per warp once all its lanes' loads
+      // are done, instead of 128 arrivals on one shared word)
       auto acc_release = [&]() {
         tc_fence_before();
-        mbar_arrive(&acc_empty[ab]);
+        if constexpr (L::kAlt) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        } else {
+          mbar_arrive(&acc_empty[ab]);
+        }
         if (++ab == kAcc) { ab = 0; aph ^= 1; }
       };
 
@@ -1197,45 +1206,34 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
         if constexpr (L::kOneHot) {
           // Count the point in this warpgroup's shared counts (warp-aggregated
-          // atomics), then write the warp's 32 columns of the tile's one-hot
-          // operand once the sums MMAs of the previous tile are done with it.
-          // The warp rewrites its points' whole columns (zeros, then 1 at
-          // (label, point)), so nothing of the previous tile survives, whichever
-          // warpgroup wrote it.  Lane -> 16-byte unit u (8 points) and rows
-          // 8i + c: every 8 consecutive lanes cover the eight 16-byte positions
-          // of the swizzled 128-byte rows (conflict-free stores).
+          // atomics), then mark it in the warpgroup's one-hot buffer once the
+          // sums MMAs of the warpgroup's previous tile are done with it: clear
+          // the element this thread set there, set (label, point) to 1.
           const int lab = valid ? idx : -1;
           int* hist = reinterpret_cast<int*>(smem + L::hist_off) + wg * 128;
           const unsigned grp = __match_any_sync(0xffffffffu, lab);
           if (lab >= 0 && lane == __ffs(grp) - 1) atomicAdd(hist + lab, __popc(grp));
-          // tile u's sums MMAs arrive on oh_empty[u & 1]: waiting for tile
-          // it-1 (the other warpgroup's) on its own barrier is at most one
-          // phase ahead, since this warpgroup saw tile it-3 consumed before
-          // writing tile it-2
-          if (it > 0) {
-            const bool got2 = mbar_wait(&oh_empty[(it - 1) & 1], static_cast<uint32_t>(((it - 1) >> 1) & 1),
-                                        abort_flag, p.status, FK_DEV_WAIT_TIMEOUT);
+          const int use = it >> 1;   // uses of this warpgroup's buffer so far
+          if (use > 0) {
+            const bool got2 = mbar_wait(&oh_empty[wg], static_cast<uint32_t>((use - 1) & 1), abort_flag,
+                                        p.status, FK_DEV_WAIT_TIMEOUT);
             if (!__all_sync(0xffffffffu, got2)) {
               ok = false;
               break;
             }
           }
-          uint8_t* ob = smem + L::oh_off + (row >> 6) * kXChunk;  // the warp's 64-point chunk
-          const int u = 4 * (q & 1) + (lane & 3);
-          const int c = (((lane >> 2) & 1) << 2) | (lane >> 3);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k = 8 * i + c;
-            *reinterpret_cast<uint4*>(ob + k * kChunkB + ((u ^ (k & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-          }
-          __syncwarp();
-          if (lab >= 0) {
-            const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
-            *reinterpret_cast<unsigned short*>(ob + lab * kChunkB + (((pb >> 4) ^ (lab & 7)) << 4) +
-                                               (pb & 15)) = Pack2<T>::kOne;
-          }
+          uint8_t* ob = smem + L::oh_off + wg * 2 * kXChunk + (row >> 6) * kXChunk;
+          const int pb = (row & 63) * 2;  // byte of this point within a 128-byte row
+          auto elem = [&](int k) -> unsigned short* {
+            return reinterpret_cast<unsigned short*>(ob + k * kChunkB + (((pb >> 4) ^ (k & 7)) << 4) +
+                                                     (pb & 15));
+          };
+          if (prev_lab >= 0) *elem(prev_lab) = 0;
+          if (lab >= 0) *elem(lab) = Pack2<T>::kOne;
+          prev_lab = lab;
           fence_proxy_async_smem();
-          mbar_arrive(&oh_full[0]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&oh_full[wg]);   // one arrival per warp
         }
         if constexpr (L::kSumWarps && XRES) {
           // hand the label (or -1 past N) to the sum warps
@@ -1300,9 +1298,24 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
             if (row < p.K) {
               const int d0 = half * 64;
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) {
-                if (d0 + jj < p.D) atomicAdd(dst + d0 + jj, __uint_as_float(sa[jj]));
-                if (d0 + 32 + jj < p.D) atomicAdd(dst + d0 + 32 + jj, __uint_as_float(sb[jj]));
+              for (int jj = 0; jj < 32; jj += 4) {
+                if (p.sums_vec) {   // D % 4 == 0: whole float4 groups, 16-byte aligned
+                  if (d0 + jj < p.D)
+                    atomicAdd(reinterpret_cast<float4*>(dst + d0 + jj),
+                              make_float4(__uint_as_float(sa[jj]), __uint_as_float(sa[jj + 1]),
+                                          __uint_as_float(sa[jj + 2]), __uint_as_float(sa[jj + 3])));
+                  if (d0 + 32 + jj < p.D)
+                    atomicAdd(reinterpret_cast<float4*>(dst + d0 + 32 + jj),
+                              make_float4(__uint_as_float(sb[jj]), __uint_as_float(sb[jj + 1]),
+                                          __uint_as_float(sb[jj + 2]), __uint_as_float(sb[jj + 3])));
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    if (d0 + jj + e < p.D) atomicAdd(dst + d0 + jj + e, __uint_as_float(sa[jj + e]));
+                    if (d0 + 32 + jj + e < p.D)
+                      atomicAdd(dst + d0 + 32 + jj + e, __uint_as_float(sb[jj + e]));
+                  }
+                }
               }
             }
           }
