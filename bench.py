@@ -374,15 +374,22 @@ def run_ours(args, rank, world, local_rank):
     a0 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     a1 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
 
-    def one_step(i=None):
-        eng.step(ev_assign=(a0[i], a1[i]) if i is not None else None)
-        shift, code = eng.read_stat()   # the reference's per-iteration `shift < tol` check
-        if code:
-            raise RuntimeError(f"device status {code}")
+    def iterations(n, timed):
+        """n Lloyd iterations as the drivers run them (LloydEngine.run): each
+        iteration's (shift, status) is read back on the host - the reference's
+        per-iteration `shift < tol` check - after the next one is queued."""
+        k0 = eng.iteration
+        eng.step(ev_assign=(a0[0], a1[0]) if timed else None)
+        for i in range(n):
+            if i + 1 < n:
+                eng.advance()
+                eng.step(ev_assign=(a0[i + 1], a1[i + 1]) if timed else None)
+            shift, code = eng.read_stat_of(k0 + i)
+            if code:
+                raise RuntimeError(f"device status {code}")
         eng.advance()
 
-    for _ in range(warm):
-        one_step()
+    iterations(warm, False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -390,8 +397,7 @@ def run_ours(args, rank, world, local_rank):
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clk:
         e0.record()
-        for i in range(steps):
-            one_step(i)
+        iterations(steps, True)
         e1.record()
         torch.cuda.synchronize()
     if world > 1:

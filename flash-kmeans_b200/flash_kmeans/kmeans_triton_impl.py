@@ -12,10 +12,11 @@ operand and c_sq staged by one small kernel, then labels with the points' rows
 and counts added to the per-cluster sums in the same pass over x whenever x is
 16-bit with D <= 128) and fk_centroid_finalize (means, next ||c||^2, shift),
 whose two stream-ordered memsets zero the accumulators for the next
-iteration.  The host reads the 8-byte
-(shift, status) record only when ``tol > 0`` or ``verbose`` needs it; with
-``tol <= 0`` the shift can never be below tol, so iterations are queued back
-to back with no host synchronisation.
+iteration.  The host reads the 8-byte (shift, status) record only when
+``tol > 0`` or ``verbose`` needs it, and then only after the next iteration
+is queued (``LloydEngine.run``); with ``tol <= 0`` the shift can never be
+below tol, so iterations are queued back to back with no host
+synchronisation.
 """
 from __future__ import annotations
 
@@ -31,7 +32,7 @@ def _round_tol(tol: float, dtype: torch.dtype) -> float:
 
 
 # Runs of at least this many iterations replay their steps from CUDA graphs:
-# capture costs about as much host time as 50 eager steps save.
+# capture costs about as much host time as 50-75 eager steps save.
 _GRAPH_MIN_ITERS = 64
 
 
@@ -39,8 +40,13 @@ class LloydEngine:
     """Buffers and launches for batched Lloyd iterations on one device.
 
     Reusable across fits of the same shape: ``load(x, centroids)`` then
-    ``step()`` per iteration.  ``ids`` always holds the last labels and
-    ``centroids`` the centroids that produced them.
+    ``step()`` per iteration and ``advance()`` to adopt its centroids.
+    Iteration k reads centroid buffer k % 3, writes buffer (k+1) % 3 and label
+    buffer k % 3, and copies its (shift, status) record to pinned host slot
+    k % 2, so iteration k+1 can run while the host checks iteration k's shift
+    without touching the labels or centroids iteration k would return
+    (``run``).  ``c_cur`` / ``c_nxt`` / ``ids`` are the current iteration's
+    buffers.
     """
 
     def __init__(self, B: int, N: int, K: int, D: int, dtype: torch.dtype, device,
@@ -48,23 +54,27 @@ class LloydEngine:
         """``metric``: "euclid" (nearest centroid, mean update) or "dot"
         (largest dot product, L2-normalised mean update: the cosine and
         dot-product k-means of the reference).  ``use_graphs``: replay the
-        steady-state step as CUDA graphs (see ``step``); capturing the two
-        pairs costs about 1.5 ms, so it pays for long runs only."""
+        steady-state step as CUDA graphs (see ``step``); capturing the three
+        pairs (one per centroid buffer) costs a few ms of host time, so it pays
+        for long runs only."""
         if metric not in ("euclid", "dot"):
             raise ValueError(f"unknown metric {metric!r}")
         self.metric = metric
         self.B, self.N, self.K, self.D, self.dtype = B, N, K, D, dtype
         self.device = torch.device(device)
         dev = self.device
-        self.c_cur = _ops.empty_rows(B, K, D, dtype, dev)
-        self.c_nxt = _ops.empty_rows(B, K, D, dtype, dev)
-        self.ids = torch.empty((B, N), dtype=torch.int32, device=dev)
+        self._cbuf = [_ops.empty_rows(B, K, D, dtype, dev) for _ in range(3)]
+        self._ibuf = [torch.empty((B, N), dtype=torch.int32, device=dev) for _ in range(3)]
+        self._k = 0   # current iteration: reads _cbuf[k % 3]
         self.sums = torch.empty((B, K, D), dtype=torch.float32, device=dev)
         self.hist = torch.empty((B, K), dtype=torch.int32, device=dev)
         self.csq = torch.empty((B, K), dtype=torch.float32, device=dev)
-        # [0] shift (float32 bits), [1] device status, [2..3] spare
+        # [0] shift (float32 bits), [1] device status, [2..3] spare; each step
+        # copies it to pinned slot k % 2 and records that slot's event
         self.stat = torch.zeros(4, dtype=torch.int32, device=dev)
-        self.stat_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        self.stat_host = torch.zeros((2, 4), dtype=torch.int32, pin_memory=True)
+        self._stat_ev = [torch.cuda.Event(), torch.cuda.Event()]
+        self._stat_k = [-1, -1]   # iteration whose record each slot holds
         self.csq_valid = False
         lib = nat.load()
         ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype))
@@ -89,11 +99,34 @@ class LloydEngine:
             return {nat.FK_ACC_PRIVATISED: 3, nat.FK_ACC_FUSED: 2}.get(method, 5)
         return {nat.FK_ACC_PRIVATISED: 4, nat.FK_ACC_FUSED: 3}.get(method, 6)
 
+    # ------------------------------------------------------------ buffers
+    @property
+    def c_cur(self) -> torch.Tensor:
+        """Centroids the current iteration assigns with."""
+        return self._cbuf[self._k % 3]
+
+    @property
+    def c_nxt(self) -> torch.Tensor:
+        """Centroids the current iteration's update writes."""
+        return self._cbuf[(self._k + 1) % 3]
+
+    @property
+    def ids(self) -> torch.Tensor:
+        """Labels of the current iteration."""
+        return self._ibuf[self._k % 3]
+
+    @property
+    def iteration(self) -> int:
+        """Index of the current iteration since ``load``."""
+        return self._k
+
     # ---------------------------------------------------------------- set-up
     def load(self, x: torch.Tensor, centroids: torch.Tensor, x_sq: torch.Tensor | None = None):
         self.x = _ops.ensure_tma(x)
         if self.metric == "euclid":
             self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
+        self._k = 0
+        self._stat_k = [-1, -1]
         self.c_cur.copy_(centroids.view(self.B, self.K, self.D))
         self.csq_valid = False
         self._graphs.clear()   # captured with the previous x
@@ -114,7 +147,8 @@ class LloydEngine:
         and sets the kernels' shared-memory attributes) the two launches of a
         step replay as CUDA graphs, one pair per centroid buffer, so a step
         costs two graph launches on the host instead of argument marshalling,
-        tensor-map encoding and three to six kernel launches."""
+        tensor-map encoding and three to six kernel launches.  Every step then
+        copies its (shift, status) record to pinned slot k % 2."""
         # a caller that overwrote c_cur clears csq_valid: the Euclidean graph
         # would pass the stale c_sq, so that step runs eagerly
         if self.use_graphs and self._steps > 0 and (self.metric == "dot" or self.csq_valid):
@@ -127,6 +161,7 @@ class LloydEngine:
                     ev_assign[1].record()
                 pair[1].replay()
                 self._steps += 1
+                self._post_stat()
                 return
         if ev_assign is not None:
             ev_assign[0].record()
@@ -136,6 +171,13 @@ class LloydEngine:
         self._launch_finalize()
         self.csq_valid = True
         self._steps += 1
+        self._post_stat()
+
+    def _post_stat(self) -> None:
+        slot = self._k % 2
+        self.stat_host[slot].copy_(self.stat, non_blocking=True)
+        self._stat_ev[slot].record()
+        self._stat_k[slot] = self._k
 
     def _launch_assign(self) -> None:
         """Assignment with the per-cluster sums and counts, on the current stream."""
@@ -229,22 +271,60 @@ class LloydEngine:
 
     def advance(self) -> None:
         """Adopt the updated centroids for the next iteration."""
-        self.c_cur, self.c_nxt = self.c_nxt, self.c_cur
+        self._k += 1
 
     def read_stat(self):
-        """(shift, device status) of the last step; synchronises the stream."""
-        self.stat_host.copy_(self.stat, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        shift = self.stat_host[0:1].view(torch.float32).item()
-        code = int(self.stat_host[1].item())
-        return shift, code
+        """(shift, device status) of the last step; waits for that step."""
+        return self.read_stat_of(self._k)
+
+    def read_stat_of(self, k: int):
+        """(shift, device status) of iteration k, one of the last two
+        iterations stepped; waits until its record has reached the host."""
+        slot = k % 2
+        if self._stat_k[slot] != k:
+            raise RuntimeError(f"no (shift, status) record of iteration {k}")
+        self._stat_ev[slot].synchronize()
+        row = self.stat_host[slot]
+        return row[0:1].view(torch.float32).item(), int(row[1].item())
+
+    def run(self, max_iters: int, tol: float, need_sync: bool, verbose_fmt: str | None = None):
+        """Lloyd iterations from the loaded centroids until ``max_iters`` or a
+        shift below ``tol`` (read only when ``need_sync``); returns (labels,
+        centroids, iterations) with the reference's break semantics: on a
+        break the labels of that iteration and the centroids that produced
+        them, else the last labels and the last update's centroids.
+
+        Iteration it+1 is queued before iteration it's shift is read: it
+        writes the other ring buffers, so the device does not wait on the
+        host's check, and a break discards it (one speculative iteration of
+        device work at convergence)."""
+        self.step()
+        for it in range(max_iters):
+            if it + 1 < max_iters:
+                self.advance()
+                self.step()
+            if need_sync:
+                shift, code = self.read_stat_of(it)
+                self.raise_on_status(code)
+                if verbose_fmt is not None:
+                    print(verbose_fmt.format(it=it, shift=shift))
+                if shift < tol:
+                    return self._ibuf[it % 3], self._contiguous(self._cbuf[it % 3]), it + 1
+        last = max_iters - 1
+        if not need_sync:
+            _, code = self.read_stat_of(last)
+            self.raise_on_status(code)
+        return self._ibuf[last % 3], self._contiguous(self._cbuf[(last + 1) % 3]), max_iters
 
     def raise_on_status(self, code: int) -> None:
         if code:
             raise RuntimeError(f"flash_kmeans device error {code}: {nat.device_status_message(code)}")
 
     def result_centroids(self) -> torch.Tensor:
-        c = self.c_cur
+        return self._contiguous(self.c_cur)
+
+    @staticmethod
+    def _contiguous(c: torch.Tensor) -> torch.Tensor:
         return c if c.is_contiguous() else c.contiguous()
 
 
@@ -287,23 +367,8 @@ def batch_kmeans_Euclid(
     with torch.cuda.device(x.device):
         eng = LloydEngine(B, N, K, D, x.dtype, x.device, use_graphs=max_iters >= _GRAPH_MIN_ITERS)
         eng.load(x, centroids)
-        need_sync = tol > 0 or verbose
-        tol_r = _round_tol(tol, x.dtype)
-        it = 0
-        for it in range(max_iters):
-            eng.step()
-            if need_sync:
-                shift, code = eng.read_stat()
-                eng.raise_on_status(code)
-                if verbose:
-                    print(f"Iter {it}, center shift: {shift:.6f}")
-                if shift < tol_r:
-                    break
-            eng.advance()
-        if not need_sync:
-            _, code = eng.read_stat()
-            eng.raise_on_status(code)
-        return eng.ids, eng.result_centroids(), it + 1
+        return eng.run(max_iters, _round_tol(tol, x.dtype), tol > 0 or verbose,
+                       "Iter {it}, center shift: {shift:.6f}" if verbose else None)
 
 
 def _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verbose, cosine):
@@ -327,24 +392,9 @@ def _batch_kmeans_similarity(x, n_clusters, max_iters, tol, init_centroids, verb
         eng = LloydEngine(B, N, K, D, x.dtype, x.device, metric="dot",
                           use_graphs=max_iters >= _GRAPH_MIN_ITERS)
         eng.load(xs, centroids)
-        need_sync = tol > 0 or verbose
-        tol_r = _round_tol(tol, x.dtype)
-        it = 0
-        for it in range(max_iters):
-            eng.step()
-            if need_sync:
-                shift, code = eng.read_stat()
-                eng.raise_on_status(code)
-                if verbose:
-                    tag = "" if cosine else " (dot)"
-                    print(f"Iter {it}{tag}, center shift: {shift:.6f}")
-                if shift < tol_r:
-                    break
-            eng.advance()
-        if not need_sync:
-            _, code = eng.read_stat()
-            eng.raise_on_status(code)
-        return eng.ids, eng.result_centroids(), it + 1
+        tag = "" if cosine else " (dot)"
+        return eng.run(max_iters, _round_tol(tol, x.dtype), tol > 0 or verbose,
+                       f"Iter {{it}}{tag}, center shift: {{shift:.6f}}" if verbose else None)
 
 
 def batch_kmeans_Cosine(x, n_clusters, max_iters=100, tol=0.0, init_centroids=None, verbose=False):
