@@ -219,7 +219,7 @@ class ClockSampler:
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x2: "applications_clocks_setting"}
 
-    def __init__(self, torch_device, period_s=0.005):
+    def __init__(self, torch_device, period_s=0.001):
         self.samples = []
         self.reasons = 0
         self.max_mhz = None
@@ -240,15 +240,23 @@ class ClockSampler:
             self.error = repr(e)
         self._t = threading.Thread(target=self._run, daemon=True)
 
-    def _run(self):
+    def _sample(self, power):
         nv = self._nv
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            if power:
                 self.power_w.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
-            except Exception:
-                pass
+        except Exception:
+            pass
+
+    def _run(self):
+        # clock and throttle reasons on every pass, power on every 8th: each
+        # NVML query takes a while, and the timed regions are short
+        i = 0
+        while not self._stop.is_set():
+            self._sample(i % 8 == 0)
+            i += 1
             time.sleep(self.period)
 
     def __enter__(self):
@@ -260,6 +268,7 @@ class ClockSampler:
         self._stop.set()
         if self._h is not None:
             self._t.join()
+            self._sample(True)   # the end of the timed region, with the device still warm
 
     def summary(self):
         if self._h is None:
