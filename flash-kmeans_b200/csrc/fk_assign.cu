@@ -635,7 +635,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       mbar_init(&c_empty[s], 1);
       mbar_init(&conv_full[s], kConvWarps * 32);
     }
-    mbar_init(final_bar, 1);
+    mbar_init(final_bar, L::kOneHot ? 2 : 1);   // one commit per MMA-issuing thread
     for (int i = 0; i < 2; ++i) {
       mbar_init(&oh_full[i], 4);
       mbar_init(&oh_empty[i], 1);
@@ -762,51 +762,6 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
       uint32_t aph = 0;
       int bi = -1, prev_b = -1;  // RESC: as in the producer
       bool ok = true;
-      // One-hot accumulation: the sums MMAs of tile t run once the epilogue
-      // has written the labels of t as a one-hot operand:
-      // sums[k][d] += sum_p onehot[k][p] * x[p][d] into the TMEM sums columns,
-      // A = one-hot (K-major: points contiguous per centroid), B = the tile's
-      // x buffer read MN-major (dims contiguous per point; LBO = the 64-dim
-      // chunk stride, SBO = 8 points).  A batch's last tile commits sums_full
-      // (sums_full_odd for the CTA's odd batches); the next batch's first sums
-      // MMA waits until the epilogue has read them (sums_empty).
-      int pt = -1, pxb = 0;       // tile whose sums MMAs are pending, its x buffer
-      int ohn = 0, fln = 0;       // one-hot buffers consumed, flushes done
-      bool sums_on = false;       // the current batch's sums already started
-      auto sums_mma = [&](int tt, int xbuf) -> bool {
-        if constexpr (L::kOneHot) {
-          constexpr uint32_t idesc_s = instr_desc(Elem<T>::kMmaFmt, kRows, 128) | (1u << 16);
-          if (!sums_on && fln > 0) {
-            if (!mbar_wait(sums_empty, static_cast<uint32_t>((fln - 1) & 1), abort_flag, p.status,
-                           FK_DEV_WAIT_TIMEOUT))
-              return false;
-            tc_fence_after();
-          }
-          const int par = ohn & 1;   // tile ohn of the CTA: its warpgroup's buffer
-          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn >> 1) & 1), abort_flag,
-                         p.status, FK_DEV_WAIT_TIMEOUT))
-            return false;
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + L::oh_off + par * 2 * kXChunk);
-          const uint32_t b0 = smem_u32(smem + L::x_off + xbuf * kResidentChunks * kXChunk);
-#pragma unroll
-          for (int s = 0; s < 8; ++s)   // 16 points per MMA
-            mma_f16(tmem_base + static_cast<uint32_t>(L::kSumsCol),
-                    smem_desc_sw128(a0 + (s >> 2) * kXChunk + (s & 3) * 32),
-                    smem_desc_sw128_mn(b0 + s * 16 * kChunkB, kXChunk, 1024), idesc_s,
-                    (sums_on || s > 0) ? 1u : 0u);
-          sums_on = true;
-          mma_commit(&oh_empty[par]);
-          mma_commit(&x_empty[xbuf]);
-          ++ohn;
-          if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
-            mma_commit((fln & 1) ? sums_full_odd : sums_full);
-            ++fln;
-            sums_on = false;
-          }
-        }
-        return true;
-      };
       if constexpr (!L::kOneHot) {
       for (int t = t_begin; ok && t < t_end; ++t) {
         bool new_batch = false, last_of_batch = false;
@@ -880,101 +835,120 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
         }
         if constexpr (XRES) {
           if (ok) {
-            if constexpr (L::kOneHot) {
-              if (pt >= 0 && !sums_mma(pt, pxb)) {
-                ok = false;
-                break;
-              }
-              pt = t;
-              pxb = xb;
-            } else {
-              mma_commit(&x_empty[xb]);
-            }
+            mma_commit(&x_empty[xb]);
             if (++xb == L::XB) { xb = 0; xph ^= 1; }
           }
         }
       }
       } else {
-        // One-hot form (K <= 128: one centroid tile, resident): the thread
-        // polls both queues and issues whatever is ready - a tile's
-        // assignment MMAs as soon as its x tile and an accumulator are free
-        // (up to kAcc tiles ahead of the epilogue), the sums MMAs of the
-        // oldest labelled tile as soon as its one-hot operand is written - so
-        // the next assignment never waits behind a one-hot tile.
-        int td = t_begin;     // next tile for the assignment MMAs (x buffer xb)
-        int ts = t_begin;     // next tile for the sums MMAs
-        int xs = 0;           // x buffer of tile ts
-        uint64_t idle0 = 0;   // when polling started to make no progress
-        while (ok && ts < t_end) {
-          bool prog = false;
-          if (td < t_end && mbar_test_wait(&x_full[xb], xph) &&
-              mbar_test_wait(&acc_empty[ab], aph ^ 1)) {
-            tc_fence_after();
-            const int b = td / p.ntn;
-            const bool new_batch = b != prev_b;
-            if (new_batch) {
-              ++bi;
-              prev_b = b;
-            }
-            const bool last_of_batch = td + 1 == t_end || (td + 1) / p.ntn != b;
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
-            for (int dc = 0; dc < p.nd; ++dc) {
-              if (new_batch && !mbar_wait(&c_full[dc], static_cast<uint32_t>(bi & 1), abort_flag,
-                                          p.status, FK_DEV_WAIT_TIMEOUT)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t a_addr =
-                  smem_u32(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk);
-              const uint32_t b_addr = smem_u32(smem + L::stages_off + dc * L::stage_bytes + L::st_c);
-#pragma unroll
-              for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t off = static_cast<uint32_t>(ks * 32);
-                mma_f16(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off), idesc,
-                        (dc > 0 || ks > 0) ? 1u : 0u);
-              }
-              if (last_of_batch) mma_commit(&c_empty[dc]);
-            }
-            if (!ok) break;
-            mma_commit(&acc_full[ab]);
-            if (++ab == kAcc) { ab = 0; aph ^= 1; }
-            if (++xb == L::XB) { xb = 0; xph ^= 1; }
-            ++td;
-            prog = true;
+        // One-hot form (K <= 128: one centroid tile, resident): this thread
+        // issues the assignment MMAs only; warp 2 issues the sums MMAs, so the
+        // two instruction streams do not wait behind each other.  A tile's x
+        // buffer is released by its sums MMAs (its assignment MMAs are done
+        // before its labels, hence its one-hot operand, exist).
+        for (int td = t_begin; ok && td < t_end; ++td) {
+          if (!mbar_wait(&x_full[xb], xph, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT) ||
+              !mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, p.status, FK_DEV_WAIT_TIMEOUT)) {
+            ok = false;
+            break;
           }
-          if (ts < td && mbar_test_wait(&oh_full[ohn & 1], static_cast<uint32_t>((ohn >> 1) & 1))) {
-            if (!sums_mma(ts, xs)) {
+          tc_fence_after();
+          const int b = td / p.ntn;
+          const bool new_batch = b != prev_b;
+          if (new_batch) {
+            ++bi;
+            prev_b = b;
+          }
+          const bool last_of_batch = td + 1 == t_end || (td + 1) / p.ntn != b;
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
+          for (int dc = 0; dc < p.nd; ++dc) {
+            if (new_batch && !mbar_wait(&c_full[dc], static_cast<uint32_t>(bi & 1), abort_flag,
+                                        p.status, FK_DEV_WAIT_TIMEOUT)) {
               ok = false;
               break;
             }
-            if (++xs == L::XB) xs = 0;
-            ++ts;
-            prog = true;
+            tc_fence_after();
+            const uint32_t a_addr =
+                smem_u32(smem + L::x_off + (xb * kResidentChunks + dc) * kXChunk);
+            const uint32_t b_addr = smem_u32(smem + L::stages_off + dc * L::stage_bytes + L::st_c);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint32_t off = static_cast<uint32_t>(ks * 32);
+              mma_f16(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off), idesc,
+                      (dc > 0 || ks > 0) ? 1u : 0u);
+            }
+            if (last_of_batch) mma_commit(&c_empty[dc]);
           }
-          if (prog) {
-            idle0 = 0;
-            continue;
-          }
-          if (*abort_flag) {
-            ok = false;
-            break;
-          }
-          const uint64_t now = globaltimer_ns();
-          if (idle0 == 0) {
-            idle0 = now;
-          } else if (now - idle0 > FK_WAIT_LIMIT_NS) {
-            *abort_flag = FK_DEV_WAIT_TIMEOUT;
-            if (p.status) atomicCAS(p.status, 0, FK_DEV_WAIT_TIMEOUT);
-            ok = false;
-            break;
-          }
-          __nanosleep(20);
+          if (!ok) break;
+          mma_commit(&acc_full[ab]);
+          if (++ab == kAcc) { ab = 0; aph ^= 1; }
+          if (++xb == L::XB) { xb = 0; xph ^= 1; }
         }
       }
       // All MMAs this thread issued must finish before TMEM is released.
       mma_commit(final_bar);
       drain_wait(final_bar, 0, 1000000000ull);
+    }
+  } else if (L::kOneHot && warp == 2) {
+    // --------------------------------------------- sums MMAs (one-hot form)
+    setmaxnreg_dec<L::kCtlRegs>();
+    if constexpr (L::kOneHot) {
+    if (lane == 0) {
+      bool ok = true;
+      // One-hot accumulation: the sums MMAs of tile t run once the epilogue
+      // has written the labels of t as a one-hot operand:
+      // sums[k][d] += sum_p onehot[k][p] * x[p][d] into the TMEM sums columns,
+      // A = one-hot (K-major: points contiguous per centroid), B = the tile's
+      // x buffer read MN-major (dims contiguous per point; LBO = the 64-dim
+      // chunk stride, SBO = 8 points).  A batch's last tile commits sums_full
+      // (sums_full_odd for the CTA's odd batches); the next batch's first sums
+      // MMA waits until the epilogue has read them (sums_empty).
+      int ohn = 0, fln = 0;       // one-hot buffers consumed, flushes done
+      bool sums_on = false;       // the current batch's sums already started
+      auto sums_mma = [&](int tt, int xbuf) -> bool {
+        {
+          constexpr uint32_t idesc_s = instr_desc(Elem<T>::kMmaFmt, kRows, 128) | (1u << 16);
+          if (!sums_on && fln > 0) {
+            if (!mbar_wait(sums_empty, static_cast<uint32_t>((fln - 1) & 1), abort_flag, p.status,
+                           FK_DEV_WAIT_TIMEOUT))
+              return false;
+            tc_fence_after();
+          }
+          const int par = ohn & 1;   // tile ohn of the CTA: its warpgroup's buffer
+          if (!mbar_wait(&oh_full[par], static_cast<uint32_t>((ohn >> 1) & 1), abort_flag,
+                         p.status, FK_DEV_WAIT_TIMEOUT))
+            return false;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + L::oh_off + par * 2 * kXChunk);
+          const uint32_t b0 = smem_u32(smem + L::x_off + xbuf * kResidentChunks * kXChunk);
+#pragma unroll
+          for (int s = 0; s < 8; ++s)   // 16 points per MMA
+            mma_f16(tmem_base + static_cast<uint32_t>(L::kSumsCol),
+                    smem_desc_sw128(a0 + (s >> 2) * kXChunk + (s & 3) * 32),
+                    smem_desc_sw128_mn(b0 + s * 16 * kChunkB, kXChunk, 1024), idesc_s,
+                    (sums_on || s > 0) ? 1u : 0u);
+          sums_on = true;
+          mma_commit(&oh_empty[par]);
+          mma_commit(&x_empty[xbuf]);
+          ++ohn;
+          if (tt + 1 == t_end || (tt + 1) / p.ntn != tt / p.ntn) {
+            mma_commit((fln & 1) ? sums_full_odd : sums_full);
+            ++fln;
+            sums_on = false;
+          }
+        }
+        return true;
+      };
+      int xs = 0;   // x buffer of tile ts
+      for (int ts = t_begin; ok && ts < t_end; ++ts) {
+        ok = sums_mma(ts, xs);
+        if (++xs == L::XB) xs = 0;
+      }
+      (void)ok;
+      // All MMAs this thread issued must finish before TMEM is released.
+      mma_commit(final_bar);
+      drain_wait(final_bar, 0, 1000000000ull);
+    }
     }
   } else if (warp < kEpiWarp0) {
     // idle warps of warpgroup 0: straight to the final barrier
