@@ -38,35 +38,53 @@ __global__ void row_sqnorm_kernel(const T* __restrict__ x, int64_t sxb, int64_t 
 // Vector path: rows of 16-byte aligned records, LPR = D * sizeof(T) / 16
 // lanes per row (a power of two <= 32), so one warp covers 32 / LPR rows per
 // step with one 16-byte load per lane; the lanes of a row combine their
-// partial sums with a segmented shuffle tree.
-template <typename T, bool SAME, int LPR>
+// partial sums with a segmented shuffle tree.  Each warp issues the loads of
+// kSteps steps before reducing any of them (bytes in flight for an HBM-bound
+// pass), and FLAT (batches laid out back to back in x and out) addresses
+// row r directly instead of dividing it into (batch, point).
+template <typename T, bool SAME, int LPR, bool FLAT>
 __global__ void row_sqnorm_vec_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn,
                                       void* out, int out_dtype, int64_t sob, int64_t son, int N,
                                       int64_t rows) {
   constexpr int E = 16 / sizeof(T);  // elements per lane
   constexpr int RPW = 32 / LPR;      // rows per warp step
+  constexpr int kSteps = 4;
   const int lane = threadIdx.x & 31;
   const int sub = lane / LPR, part = lane % LPR;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t step = warps * RPW;
+  auto xoff = [&](int64_t r) -> int64_t {
+    if constexpr (FLAT) return r * sxn;
+    const int64_t b = r / N;
+    return b * sxb + (r - b * N) * sxn;
+  };
+  auto ooff = [&](int64_t r) -> int64_t {
+    if constexpr (FLAT) return r * son;
+    const int64_t b = r / N;
+    return b * sob + (r - b * N) * son;
+  };
   for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
-       r0 < rows; r0 += warps * RPW) {
-    const int64_t r = r0 + sub;
-    float acc = 0.0f;
-    if (r < rows) {
-      const int64_t b = r / N, n = r % N;
-      const uint4 v = *reinterpret_cast<const uint4*>(x + b * sxb + n * sxn + part * E);
-      const T* e = reinterpret_cast<const T*>(&v);
+       r0 < rows; r0 += step * kSteps) {
+    uint4 v[kSteps];
+#pragma unroll
+    for (int u = 0; u < kSteps; ++u) {
+      const int64_t r = r0 + u * step + sub;
+      v[u] = r < rows ? __ldcs(reinterpret_cast<const uint4*>(x + xoff(r) + part * E))
+                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kSteps; ++u) {
+      const int64_t r = r0 + u * step + sub;
+      float acc = 0.0f;
+      const T* e = reinterpret_cast<const T*>(&v[u]);
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const float f = Elem<T>::to_f(e[i]);
         acc += SAME ? Elem<T>::round(f * f) : f * f;
       }
-    }
 #pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (part == 0 && r < rows) {
-      const int64_t b = r / N, n = r % N;
-      store_f(out, b * sob + n * son, out_dtype, acc);
+      for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (part == 0 && r < rows) store_f(out, ooff(r), out_dtype, acc);
     }
   }
 }
@@ -129,19 +147,27 @@ static int row_sqnorm_typed(const void* x, int dtype, int64_t B, int64_t N, int6
                    (B == 1 || (xs[0] * eb) % 16 == 0);
   if (vec) {
     const bool same = out_dtype == dtype;
+    const bool flat = (B == 1 || xs[0] == N * xs[1]) && (B == 1 || os[0] == N * os[1]);
     const T* xt = static_cast<const T*>(x);
+#define FK_SQN2(L, F)                                                                             \
+  if (same)                                                                                       \
+    row_sqnorm_vec_kernel<T, true, L, F><<<static_cast<int>(blocks), threads, 0, s>>>(            \
+        xt, xs[0], xs[1], out, out_dtype, os[0], os[1], static_cast<int>(N), rows);               \
+  else                                                                                            \
+    row_sqnorm_vec_kernel<T, false, L, F><<<static_cast<int>(blocks), threads, 0, s>>>(           \
+        xt, xs[0], xs[1], out, out_dtype, os[0], os[1], static_cast<int>(N), rows);
 #define FK_SQN(L)                                                                                 \
   if (lpr == L) {                                                                                 \
-    if (same)                                                                                     \
-      row_sqnorm_vec_kernel<T, true, L><<<static_cast<int>(blocks), threads, 0, s>>>(             \
-          xt, xs[0], xs[1], out, out_dtype, os[0], os[1], static_cast<int>(N), rows);             \
-    else                                                                                          \
-      row_sqnorm_vec_kernel<T, false, L><<<static_cast<int>(blocks), threads, 0, s>>>(            \
-          xt, xs[0], xs[1], out, out_dtype, os[0], os[1], static_cast<int>(N), rows);             \
+    if (flat) {                                                                                   \
+      FK_SQN2(L, true)                                                                            \
+    } else {                                                                                      \
+      FK_SQN2(L, false)                                                                           \
+    }                                                                                             \
     return check_launch("row_sqnorm_vec_kernel");                                               \
   }
     FK_SQN(1) FK_SQN(2) FK_SQN(4) FK_SQN(8) FK_SQN(16) FK_SQN(32)
 #undef FK_SQN
+#undef FK_SQN2
   }
   if (out_dtype == dtype)
     row_sqnorm_kernel<T, true><<<static_cast<int>(blocks), threads, 0, s>>>(

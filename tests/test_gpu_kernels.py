@@ -51,6 +51,24 @@ def test_row_sqnorm_matches_oracle(fk, dt, D):
         assert (got != want).mean() < 0.02
 
 
+@pytest.mark.parametrize("dt", ["float16", "float32"])
+def test_row_sqnorm_layouts_agree(fk, dt):
+    """The vector kernel addresses rows directly when batches are back to back and
+    through (batch, point) otherwise; both give the same bits, over enough rows that
+    every warp runs several unrolled iterations and a ragged tail."""
+    from flash_kmeans import _ops
+    B, N, D = 3, 100003, 64
+    big = torch.randn((B, N + 5, D), device="cuda").to(TD[dt])
+    strided = big[:, :N]                      # batch stride (N+5)*D: the (batch, point) path
+    flat = strided.contiguous()
+    a = _ops.row_sqnorm(strided)
+    b = _ops.row_sqnorm(flat)
+    assert torch.equal(a, b)
+    want = ko.row_sqnorm(_np(flat[:, :2000]), dt)
+    rel = np.abs(_np(b[:, :2000]) - want) / np.maximum(np.abs(want), 1e-6)
+    assert rel.max() <= {"float16": 2 ** -10, "float32": 1e-5}[dt] * 1.01
+
+
 # ----------------------------------------------------------------- assignment
 @pytest.mark.parametrize("spec", cases.ASSIGN_CASES, ids=lambda s: s["name"])
 def test_assign_matches_golden_and_oracle(fk, spec):
