@@ -1500,6 +1500,38 @@ __global__ void prep_centroids_kernel(const T* __restrict__ c, int64_t scb, int6
   }
 }
 
+// c_sq given, 16-bit centroids stored densely (rows of D elements back to
+// back, D a multiple of 8, 16-byte aligned): the -2c operand 16 bytes per
+// thread step (the same per-element saturated -2e as prep_centroids_kernel),
+// then the padded c_sq copy.  This is the Lloyd engine's steady state.
+template <typename T, int MODE>
+__global__ void prep_centroids_flat_kernel(const T* __restrict__ c, T* __restrict__ cneg,
+                                           int64_t units, const void* __restrict__ csq_in,
+                                           int csq_dtype, int64_t sqb, int64_t sqk,
+                                           void* __restrict__ csq_out, int64_t kpad, int K,
+                                           int64_t csq_total) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t u = tid; u < units; u += nth) {
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(c) + u);
+    T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      e[i] = Elem<T>::from_f(fminf(fmaxf(-2.0f * Elem<T>::to_f(e[i]), -Elem<T>::kMaxFinite),
+                                   Elem<T>::kMaxFinite));
+    reinterpret_cast<uint4*>(cneg)[u] = v;
+  }
+  for (int64_t r = tid; r < csq_total; r += nth) {
+    const int64_t b = r / kpad;
+    const int k = static_cast<int>(r - b * kpad);
+    const float v = k < K ? load_f(csq_in, b * sqb + k * sqk, csq_dtype) : __int_as_float(0x7f800000);
+    if (MODE == 0)
+      static_cast<T*>(csq_out)[r] = Elem<T>::from_f(v);
+    else
+      static_cast<float*>(csq_out)[r] = v;
+  }
+}
+
 // c_sq given: one thread per padded element (convert, +inf beyond K).
 template <typename T, int MODE>
 __global__ void copy_csq_kernel(const void* __restrict__ csq_in, int csq_dtype, int64_t sqb,
@@ -1553,6 +1585,26 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
     copy_csq_kernel<T, 2><<<blocks, 256, 0, stream>>>(c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad,
                                                        (int)K, total);
     int st = check_launch("copy_csq_kernel");
+    if (st != FK_OK) return st;
+  } else if (c_sq && cneg && dp == D && cs[2] == 1 && cs[1] == D && (B == 1 || cs[0] == K * D) &&
+             reinterpret_cast<uintptr_t>(cent) % 16 == 0) {
+    // steady state of the Lloyd engine: dense centroids, c_sq from the update
+    const int64_t units = B * K * D / 8;
+    const int64_t csq_total = B * kpad;
+    const int64_t work = units > csq_total ? units : csq_total;
+    const int sms = sm_count_current();
+    const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 8 : 1024;
+    const int blocks = static_cast<int>((work + 255) / 256 < cap ? (work + 255) / 256 : cap);
+    const T* c = static_cast<const T*>(cent);
+    if constexpr (eb == 2) {   // cneg exists for 16-bit centroids only (8 per 16 bytes)
+      if (mode == 0)
+        prep_centroids_flat_kernel<T, 0><<<blocks, 256, 0, stream>>>(
+            c, cneg, units, c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad, (int)K, csq_total);
+      else
+        prep_centroids_flat_kernel<T, 1><<<blocks, 256, 0, stream>>>(
+            c, cneg, units, c_sq, csq_dtype, cqs[0], cqs[1], ws, kpad, (int)K, csq_total);
+    }
+    int st = check_launch("prep_centroids_flat_kernel");
     if (st != FK_OK) return st;
   } else {
     const int threads = 256;

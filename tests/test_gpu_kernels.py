@@ -149,20 +149,24 @@ def test_assign_strided_inputs(fk):
     assert_labels(xs, c, ids, want, "float16", "strided")
 
 
-def test_assign_out_and_csq_arguments(fk):
+@pytest.mark.parametrize("dt,xsq32", [("float16", False), ("bfloat16", False), ("float16", True)])
+def test_assign_out_and_csq_arguments(fk, dt, xsq32):
+    """out= and c_sq= arguments; with c_sq given and dense centroids the -2c operand
+    is staged by the vectorised kernel (the Lloyd engine's steady state), with it
+    absent by the per-row kernel that also computes c_sq."""
     from flash_kmeans import _ops
     from flash_kmeans.assign_euclid_triton import euclid_assign_triton
     rng = np.random.default_rng(6)
-    x = ko.round_to(rng.standard_normal((2, 700, 64), dtype=np.float32), "float16")
-    c = ko.round_to(rng.standard_normal((2, 90, 64), dtype=np.float32), "float16")
-    xd, cd = _dev(x, "float16"), _dev(c, "float16")
-    xsq = _ops.row_sqnorm(xd)
+    x = ko.round_to(rng.standard_normal((2, 700, 64), dtype=np.float32), dt)
+    c = ko.round_to(rng.standard_normal((2, 90, 64), dtype=np.float32), dt)
+    xd, cd = _dev(x, dt), _dev(c, dt)
+    xsq = (xd.float() ** 2).sum(-1) if xsq32 else _ops.row_sqnorm(xd)
     out = torch.full((2, 700), -1, dtype=torch.int32, device="cuda")
     csq = (cd.float() ** 2).sum(-1)
     r = euclid_assign_triton(xd, cd, xsq, out=out, c_sq=csq)
     assert r.data_ptr() == out.data_ptr()
     base = euclid_assign_triton(xd, cd, xsq)
-    rep = label_report(x, c, out.cpu().numpy(), base.cpu().numpy(), "float16")
+    rep = label_report(x, c, out.cpu().numpy(), base.cpu().numpy(), dt)
     assert rep["bad"] == 0
     with pytest.raises(ValueError):
         euclid_assign_triton(xd, cd, xsq, num_warps=4)
