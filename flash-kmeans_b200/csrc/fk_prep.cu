@@ -117,6 +117,91 @@ __global__ void row_normalize_kernel(const T* __restrict__ x, int64_t sxb, int64
   }
 }
 
+// Vector path of row_normalize_kernel (contiguous rows of 16-byte aligned
+// records, LPR = D * sizeof(T) / 16 lanes per row, a power of two <= 32): each
+// lane squares and sums its 16 bytes in float32, a segmented shuffle tree
+// combines the row's lanes, and the lane divides the elements it still holds.
+// Same rounding steps as the scalar kernel (float32 sum, norm rounded to the
+// dtype and clamped, one rounded division per element); the float32 summation
+// order differs, as it does from torch's.  FLAT: batches back to back.
+template <typename T, int LPR, bool FLAT>
+__global__ void row_normalize_vec_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn,
+                                         T* __restrict__ out, int64_t sob, int64_t son, int N,
+                                         int64_t rows) {
+  constexpr int E = 16 / sizeof(T);
+  constexpr int RPW = 32 / LPR;
+  constexpr int kSteps = 2;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LPR, part = lane % LPR;
+  const float eps = Elem<T>::round(1e-12f);
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t step = warps * RPW;
+  auto off = [&](int64_t r, int64_t sb, int64_t sn) -> int64_t {
+    if constexpr (FLAT) return r * sn;
+    const int64_t b = r / N;
+    return b * sb + (r - b * N) * sn;
+  };
+  for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+       r0 < rows; r0 += step * kSteps) {
+    uint4 v[kSteps];
+#pragma unroll
+    for (int u = 0; u < kSteps; ++u) {
+      const int64_t r = r0 + u * step + sub;
+      v[u] = r < rows ? __ldcs(reinterpret_cast<const uint4*>(x + off(r, sxb, sxn) + part * E))
+                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kSteps; ++u) {
+      const int64_t r = r0 + u * step + sub;
+      T* e = reinterpret_cast<T*>(&v[u]);
+      float ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const float f = Elem<T>::to_f(e[i]);
+        ss = __fmaf_rn(f, f, ss);
+      }
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float den = fmaxf(Elem<T>::round(sqrtf(ss)), eps);
+#pragma unroll
+      for (int i = 0; i < E; ++i) e[i] = Elem<T>::from_f(__fdiv_rn(Elem<T>::to_f(e[i]), den));
+      if (r < rows) __stcs(reinterpret_cast<uint4*>(out + off(r, sob, son) + part * E), v[u]);
+    }
+  }
+}
+
+template <typename T>
+static int row_normalize_vec(const void* x, int64_t B, int64_t N, int64_t D, const int64_t* xs,
+                             void* out, const int64_t* os, int64_t blocks, cudaStream_t s,
+                             bool* done) {
+  constexpr int64_t eb = sizeof(T);
+  const int64_t lpr = D * eb / 16;
+  *done = xs[2] == 1 && os[2] == 1 && (D * eb) % 16 == 0 && (lpr & (lpr - 1)) == 0 && lpr <= 32 &&
+          reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+          (xs[1] * eb) % 16 == 0 && (os[1] * eb) % 16 == 0 &&
+          (B == 1 || ((xs[0] * eb) % 16 == 0 && (os[0] * eb) % 16 == 0));
+  if (!*done) return FK_OK;
+  const bool flat = B == 1 || (xs[0] == N * xs[1] && os[0] == N * os[1]);
+  const T* xt = static_cast<const T*>(x);
+  T* ot = static_cast<T*>(out);
+  const int64_t rows = B * N;
+#define FK_RN2(L, F)                                                                              \
+  row_normalize_vec_kernel<T, L, F><<<static_cast<int>(blocks), 256, 0, s>>>(                     \
+      xt, xs[0], xs[1], ot, os[0], os[1], static_cast<int>(N), rows);
+#define FK_RN(L)                                                                                  \
+  if (lpr == L) {                                                                                 \
+    if (flat) {                                                                                   \
+      FK_RN2(L, true)                                                                             \
+    } else {                                                                                      \
+      FK_RN2(L, false)                                                                            \
+    }                                                                                             \
+  }
+  FK_RN(1) FK_RN(2) FK_RN(4) FK_RN(8) FK_RN(16) FK_RN(32)
+#undef FK_RN
+#undef FK_RN2
+  return check_launch("row_normalize_vec_kernel");
+}
+
 template <typename T>
 __global__ void pack_rows_kernel(const T* __restrict__ x, int64_t sxb, int64_t sxn, int64_t sxd,
                                  T* __restrict__ out, int N, int D, int Dp, int64_t total) {
@@ -241,6 +326,17 @@ extern "C" int fk_row_normalize(const void* x, int dtype, int64_t B, int64_t N, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t* xs = x_strides3;
   const int64_t* os = out_strides3;
+  {
+    bool done = false;
+    int st = FK_OK;
+    if (dtype == FK_F16)
+      st = row_normalize_vec<__half>(x, B, N, D, xs, out, os, blocks, s, &done);
+    else if (dtype == FK_BF16)
+      st = row_normalize_vec<__nv_bfloat16>(x, B, N, D, xs, out, os, blocks, s, &done);
+    else if (dtype == FK_F32)
+      st = row_normalize_vec<float>(x, B, N, D, xs, out, os, blocks, s, &done);
+    if (done || st != FK_OK) return st;
+  }
   switch (dtype) {
     case FK_F16:
       row_normalize_kernel<__half><<<static_cast<int>(blocks), 256, 0, s>>>(
