@@ -56,6 +56,7 @@ constexpr int kCent = 256;            // centroids per tile (MMA N); 128 for K <
 constexpr int kTmemCols = 512;        // accumulators: kTmemCols / tile width of them
 constexpr int kChunkB = 128;          // bytes per row chunk = one 128B swizzle span
 constexpr int kXChunk = kRows * kChunkB;   // 16 KB
+constexpr int kW64MinD = 512;          // float32 rows from here on take the 64-byte-row ring
 // Warpgroup 0 = TMA producer (warp 0), MMA issuer (warp 1), two idle warps;
 // warpgroups 1-2 = epilogue; warpgroup 3 (when present) = split converters or
 // sum warps.  Roles follow warpgroups so each can get its own register budget.
@@ -83,7 +84,15 @@ struct Layout {
   static constexpr bool kAlt = RESC && KC < kCent;
   static constexpr int kGroups = kAlt ? 1 : EPI / 4;  // column groups of each centroid tile
   static constexpr int kSplit = split_mode(MODE) ? 2 : 1;  // hi/lo copies for 3xTF32
-  static constexpr int kCChunk = KC * kChunkB;        // one 128-byte column chunk of a tile
+  // Rows of a chunk: 128 bytes (128-byte swizzle), or 64 bytes (64-byte
+  // swizzle) in the four-stage form of the 3xTF32 modes: their stages hold hi
+  // and lo copies of both operands, so four 64-byte-row stages fit where two
+  // 128-byte-row ones do (used for long rows, where the deeper ring hides the
+  // loads; short rows keep fewer, wider stages).
+  static constexpr int kRowB = (split_mode(MODE) && STAGES == 4) ? 64 : kChunkB;
+  static constexpr int kKSteps = kRowB / 32;           // MMA K steps (32 bytes) per chunk
+  static constexpr int kCChunk = KC * kRowB;           // one column chunk of a centroid tile
+  static constexpr int kXChunkL = kRows * kRowB;       // one column chunk of a point tile
   // Fused accumulation comes in two forms: with 256-column tiles (large K)
   // four sum warps add each point's row to its cluster's sums with vector
   // atomics; with 128-column tiles (K <= 128) the tensor core adds a one-hot
@@ -112,8 +121,8 @@ struct Layout {
   static constexpr int st_c = 0;                          // centroid chunk (hi)
   static constexpr int st_clo = kCChunk;                  // centroid chunk lo (mode 2)
   static constexpr int st_x = kCChunk * kSplit;           // x chunk (split-D)
-  static constexpr int st_xlo = st_x + kXChunk;           // x chunk lo (mode 2)
-  static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunk * kSplit);
+  static constexpr int st_xlo = st_x + kXChunkL;          // x chunk lo (mode 2)
+  static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunkL * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
   // one-hot operands [warpgroup][point chunk 0..1][centroid row][64 points],
   // 16-bit, 128-byte swizzle (K-major A operand of the sums MMA).  One buffer
@@ -731,7 +740,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                 break;
               }
               uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
-              mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : kXChunk));
+              mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : L::kXChunkL));
               tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
               if constexpr (!XRES)
                 tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
@@ -805,18 +814,19 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                      : smem_u32(st + L::st_x);
             const uint32_t b_addr = smem_u32(st + L::st_c);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < L::kKSteps; ++ks) {
               const uint32_t acc = (dc > 0 || ks > 0) ? 1u : 0u;
               const uint32_t off = static_cast<uint32_t>(ks * 32);
               if constexpr (split_mode(MODE)) {
                 const uint32_t alo = smem_u32(st + L::st_xlo);
                 const uint32_t blo = smem_u32(st + L::st_clo);
-                mma_tf32(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off),
-                         idesc, acc);
-                mma_tf32(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(blo + off), idesc,
-                         1u);
-                mma_tf32(d_tmem, smem_desc_sw128(alo + off), smem_desc_sw128(b_addr + off), idesc,
-                         1u);
+                auto sd = [](uint32_t a) {
+                  if constexpr (L::kRowB == 64) return smem_desc_sw64(a);
+                  else return smem_desc_sw128(a);
+                };
+                mma_tf32(d_tmem, sd(a_addr + off), sd(b_addr + off), idesc, acc);
+                mma_tf32(d_tmem, sd(a_addr + off), sd(blo + off), idesc, 1u);
+                mma_tf32(d_tmem, sd(alo + off), sd(b_addr + off), idesc, 1u);
               } else {
                 mma_f16(d_tmem, smem_desc_sw128(a_addr + off), smem_desc_sw128(b_addr + off),
                         idesc, acc);
@@ -1391,7 +1401,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
             }
           };
           split(L::st_c, L::st_clo, kCChunk / 16);
-          split(L::st_x, L::st_xlo, kXChunk / 16);
+          split(L::st_x, L::st_xlo, L::kXChunkL / 16);
           fence_proxy_async_smem();
           mbar_arrive(&conv_full[stage]);
           if (++stage == STAGES) { stage = 0; sph ^= 1; }
@@ -1410,13 +1420,14 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
 }
 
 // ------------------------------------------------------------------ host side
-template <typename T, int MODE, bool XRES, bool FUSE = false, int KC = kCent, bool RESC = false>
+template <typename T, int MODE, bool XRES, bool FUSE = false, int KC = kCent, bool RESC = false,
+          bool W64 = false>
 static int launch_assign(const CUtensorMap& tx, const CUtensorMap& tc, const AssignParams& p,
                          cudaStream_t stream) {
   // centroid ring depth (the narrow-tile ring holds as many bytes in twice the
   // stages; resident centroids need one stage per chunk of the batch)
   constexpr int STAGES = RESC ? kResidentChunks
-                              : (split_mode(MODE) ? 2 : (FUSE ? 3 : (KC < kCent ? 6 : 4)));
+                              : (split_mode(MODE) ? (W64 ? 4 : 2) : (FUSE ? 3 : (KC < kCent ? 6 : 4)));
   constexpr int EPI = 8;  // epilogue warps: 4 TMEM lane quarters x 2 column halves
   using L = Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC>;
   static_assert(L::total <= 232448, "shared memory budget");
@@ -1559,7 +1570,10 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   constexpr int eb = Elem<T>::kBytes;
   const bool is16 = eb == 2;
   const int mode = dot ? (is16 ? 3 : 4) : (is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2);
-  const int dch = kChunkB / eb;
+  // elements per chunk row: 128 bytes, or 64 in the four-stage 3xTF32 form
+  // (float32 rows of at least kW64MinD elements)
+  const bool w64 = !is16 && D >= kW64MinD;
+  const int dch = (w64 ? 64 : kChunkB) / eb;
   const int nd = static_cast<int>((D + dch - 1) / dch);
   const bool xres = is16 && nd <= kResidentChunks;
   // K <= 128 (one centroid tile either way): 128-column tiles, so the epilogue
@@ -1630,12 +1644,12 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
 
   // 2) tensor maps: x as (D, N, B), centroids (or -2c) as (D, K, B), 128-byte swizzle
   CUtensorMap tx, tc;
-  int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows);
+  int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows, w64);
   if (st != FK_OK) return st;
   if (cneg)
     st = encode_tmap_3d(&tc, cneg, Elem<T>::kDtype, D, K, B, dp * eb, K * dp * eb, dch, kc);
   else
-    st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc);
+    st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc, w64);
   if (st != FK_OK) return st;
 
   AssignParams p;
@@ -1675,7 +1689,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
                   : launch_assign<T, 3, false>(tx, tc, p, stream);
     } else {
       if (sums) return fail(FK_ERR_UNSUPPORTED, "fused sums need 16-bit x");
-      return launch_assign<T, 4, false>(tx, tc, p, stream);
+      return w64 ? launch_assign<T, 4, false, false, kCent, false, true>(tx, tc, p, stream)
+                 : launch_assign<T, 4, false>(tx, tc, p, stream);
     }
   }
   if constexpr (Elem<T>::kBytes == 2) {
@@ -1698,7 +1713,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
     return xres ? launch_assign<T, 1, true>(tx, tc, p, stream)
                 : launch_assign<T, 1, false>(tx, tc, p, stream);
   } else {
-    return launch_assign<T, 2, false>(tx, tc, p, stream);
+    return w64 ? launch_assign<T, 2, false, false, kCent, false, true>(tx, tc, p, stream)
+               : launch_assign<T, 2, false>(tx, tc, p, stream);
   }
 }
 

@@ -70,7 +70,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 int encode_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
-                   uint32_t box1) {
+                   uint32_t box1, bool sw64) {
   auto enc = get_encode();
   if (!enc) return fail(FK_ERR_TMA, "cuTensorMapEncodeTiled not available from the driver");
   CUtensorMapDataType dt = dtype == FK_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -82,7 +82,8 @@ int encode_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, u
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r =
       enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FK_ERR_TMA,

@@ -89,9 +89,10 @@ int current_device();
 
 // cuTensorMapEncodeTiled resolved once through the runtime's driver entry
 // point (no link-time dependency on libcuda).
+// `sw64`: the 64-byte swizzle (box rows of 64 bytes) instead of the 128-byte one.
 int encode_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
-                   uint32_t box1);
+                   uint32_t box1, bool sw64 = false);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -252,6 +252,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for rows of 64 bytes with the 64-byte swizzle: 8-row atoms of 512
+// bytes (SBO), layout type 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
+
 // Shared-memory matrix descriptor for an MN-major operand stored with the
 // 128-byte swizzle: each 128-byte row holds 64 consecutive MN elements (16-bit)
 // of one K index, 8 K rows form a 1024-byte atom; `lbo` = byte stride between
