@@ -190,6 +190,7 @@ struct AssignParams {
   int nkt;          // centroid tiles
   int total_tiles;
   int* status;
+  int lo_b;         // 3xTF32 modes: the centroids' lo halves are batches lo_b.. of tmap_c
 };
 
 __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
@@ -740,8 +741,11 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                 break;
               }
               uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
-              mbar_arrive_expect_tx(&c_full[stage], kCChunk + (XRES ? 0 : L::kXChunkL));
+              mbar_arrive_expect_tx(&c_full[stage], kCChunk * L::kSplit + (XRES ? 0 : L::kXChunkL));
               tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
+              if constexpr (split_mode(MODE))   // the centroids come split (hi, lo) per call
+                tma_load_3d(st + L::st_clo, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent,
+                            b + p.lo_b);
               if constexpr (!XRES)
                 tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
               last_par[stage] = static_cast<int>(sph);
@@ -1400,8 +1404,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
               lo[i] = vl;
             }
           };
-          split(L::st_c, L::st_clo, kCChunk / 16);
-          split(L::st_x, L::st_xlo, L::kXChunkL / 16);
+          split(L::st_x, L::st_xlo, L::kXChunkL / 16);   // the centroids arrive split
           fence_proxy_async_smem();
           mbar_arrive(&conv_full[stage]);
           if (++stage == STAGES) { stage = 0; sph ^= 1; }
@@ -1543,6 +1546,26 @@ __global__ void prep_centroids_flat_kernel(const T* __restrict__ c, T* __restric
   }
 }
 
+// 3xTF32 modes: the centroids split once per call into tf32 hi parts
+// (rounded to 10 explicit mantissa bits) and exact lo rests, each dense
+// (B, K, dp) with zero padding, lo at hi + lo_off: the split the converter
+// warps apply to the x chunks, done here once instead of for every point tile.
+__global__ void split_centroids_kernel(const float* __restrict__ c, int64_t scb, int64_t sck,
+                                       int64_t scd, float* __restrict__ hi, int64_t dp, int K,
+                                       int D, int64_t total, int64_t lo_off) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / dp;
+    const int d = static_cast<int>(i - row * dp);
+    const int64_t b = row / K;
+    const int k = static_cast<int>(row - b * K);
+    const float v = d < D ? c[b * scb + k * sck + d * scd] : 0.0f;
+    const float h = __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
+    hi[i] = h;
+    hi[lo_off + i] = v - h;
+  }
+}
+
 // c_sq given: one thread per padded element (convert, +inf beyond K).
 template <typename T, int MODE>
 __global__ void copy_csq_kernel(const void* __restrict__ csq_in, int csq_dtype, int64_t sqb,
@@ -1591,6 +1614,20 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   T* cneg = nullptr;
   if (!dot && is16)
     cneg = reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + assign_csq_bytes(B, K));
+  // float32 (3xTF32 modes): the centroids' hi and lo halves, (2B, K, dp)
+  float* csplit = nullptr;
+  if (!is16) {
+    csplit = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + assign_csq_bytes(B, K));
+    const int64_t total = B * K * dp;
+    const int sms = sm_count_current();
+    const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 8 : 1024;
+    const int blocks = static_cast<int>((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
+    split_centroids_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float*>(cent), cs[0], cs[1],
+                                                       cs[2], csplit, dp, (int)K, (int)D, total,
+                                                       total);
+    int st = check_launch("split_centroids_kernel");
+    if (st != FK_OK) return st;
+  }
   if (dot) {
     // nothing to stage
   } else if (c_sq && mode == 2) {
@@ -1648,6 +1685,8 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   if (st != FK_OK) return st;
   if (cneg)
     st = encode_tmap_3d(&tc, cneg, Elem<T>::kDtype, D, K, B, dp * eb, K * dp * eb, dch, kc);
+  else if (csplit)  // hi halves in batches [0, B), lo halves in [B, 2B)
+    st = encode_tmap_3d(&tc, csplit, Elem<T>::kDtype, D, K, 2 * B, dp * eb, K * dp * eb, dch, kc, w64);
   else
     st = encode_tmap_3d(&tc, cent, Elem<T>::kDtype, D, K, B, cs[1] * eb, cs[0] * eb, dch, kc, w64);
   if (st != FK_OK) return st;
@@ -1674,6 +1713,7 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.nkt = nkt;
   p.total_tiles = static_cast<int>(B * p.ntn);
   p.status = status;
+  p.lo_b = static_cast<int>(B);
 
   if (dot) {
     if constexpr (Elem<T>::kBytes == 2) {
@@ -1730,6 +1770,8 @@ extern "C" size_t fk_assign_workspace_size(int64_t B, int64_t K, int64_t D, int 
   size_t bytes = assign_csq_bytes(B, K);
   if (dtype == FK_F16 || dtype == FK_BF16)
     bytes += align_up(static_cast<size_t>(B * K) * align_up(static_cast<size_t>(D), 8) * 2, 256);
+  else  // float32: the centroids' tf32 hi and lo halves
+    bytes += align_up(static_cast<size_t>(B * K) * align_up(static_cast<size_t>(D), 8) * 8, 256);
   return bytes + 256;
 }
 

@@ -122,7 +122,8 @@ int fk_pack_rows(const void* x, int dtype, int64_t B, int64_t N, int64_t D,
  * the dot products are 3xTF32 on the tensor cores).  Ties resolve to the
  * lowest centroid index; a NaN distance wins at its first column, as argmin.
  * Requires K <= 1<<20, N < 2^31.  The workspace (fk_assign_workspace_size)
- * holds the padded c_sq and, for 16-bit x, -2c (about B*K*D*2 bytes). */
+ * holds the padded c_sq and, for 16-bit x, -2c (about B*K*D*2 bytes); for
+ * float32 x, the centroids' tf32 hi and lo halves (about B*K*D*8 bytes). */
 size_t fk_assign_workspace_size(int64_t B, int64_t K, int64_t D, int dtype);
 int fk_assign(const void* x, const void* centroids, const void* x_sq, const void* c_sq,
               int32_t* out, int32_t* counts, int dtype, int xsq_dtype, int csq_dtype,

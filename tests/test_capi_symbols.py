@@ -50,7 +50,9 @@ def test_host_only_entry_points(lib):
     # padded c_sq, then the -2c operand for 16-bit x (none for float32)
     assert lib.fk_assign_workspace_size(32, 1000, 128, 0) >= 32 * 1024 * 4 + 32 * 1000 * 128 * 2
     assert lib.fk_assign_workspace_size(32, 1000, 100, 1) >= 32 * 1024 * 4 + 32 * 1000 * 104 * 2
-    assert lib.fk_assign_workspace_size(32, 1000, 128, 2) < 32 * 1024 * 4 + 1024
+    # float32: the centroids' tf32 hi and lo halves (B, K, D padded to 8) besides c_sq
+    assert lib.fk_assign_workspace_size(32, 1000, 128, 2) >= 32 * 1024 * 4 + 2 * 32 * 1000 * 128 * 4
+    assert lib.fk_assign_workspace_size(32, 1000, 128, 2) < 32 * 1024 * 4 + 2 * 32 * 1000 * 128 * 4 + 2048
     assert lib.fk_centroid_accumulate_workspace_size(32, 75600, 1000) >= 2 * 32 * 75600 * 4
     st = (ctypes.c_int64 * 3)(75600 * 128, 128, 1)
     assert lib.fk_tma_compatible(ctypes.c_void_p(1 << 20), 0, 128, st) == 1
