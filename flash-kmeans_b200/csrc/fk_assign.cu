@@ -108,9 +108,9 @@ struct Layout {
   // resident x tile buffers: a third one lets the fused sum warps hold a tile,
   // or (narrow tiles, one centroid tile per point tile) lets x loads run
   // further ahead of the short per-tile MMA work; with resident centroids
-  // (RESC) the ring is small and five x tiles fit (four next to the one-hot
-  // buffer: a one-hot tile holds its x buffer until its sums MMAs finish, so
-  // the ring must cover the load latency plus two epilogue periods)
+  // (RESC) the ring is small and five x tiles fit; next to the two one-hot
+  // buffers four fit (three with the shared-memory argmin slots).  A one-hot
+  // tile holds its x buffer until its sums MMAs finish.
   // mode 0 keeps its saved chunk in registers in the one-hot form; the other
   // modes 0, 3 and 4 use shared-memory slots
   static constexpr bool kRegSave = kOneHot && MODE == 0;
@@ -119,9 +119,9 @@ struct Layout {
   static constexpr int x_off = 0;
   static constexpr int x_bytes = XRES ? XB * kResidentChunks * kXChunk : 0;
   static constexpr int st_c = 0;                          // centroid chunk (hi)
-  static constexpr int st_clo = kCChunk;                  // centroid chunk lo (mode 2)
+  static constexpr int st_clo = kCChunk;                  // centroid chunk lo (3xTF32, TMA-loaded)
   static constexpr int st_x = kCChunk * kSplit;           // x chunk (split-D)
-  static constexpr int st_xlo = st_x + kXChunkL;          // x chunk lo (mode 2)
+  static constexpr int st_xlo = st_x + kXChunkL;          // x chunk lo (3xTF32, converter warps)
   static constexpr int stage_bytes = kCChunk * kSplit + (XRES ? 0 : kXChunkL * kSplit);
   static constexpr int stages_off = x_off + x_bytes;
   // one-hot operands [warpgroup][point chunk 0..1][centroid row][64 points],
@@ -1374,6 +1374,8 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     }
   } else if (split_mode(MODE)) {
     // ------------------------------------- 3xTF32 split converters (modes 2, 4)
+    // Each stage's x chunk is split in place into tf32 hi and the exact lo
+    // rest (the centroid chunks arrive already split, from the workspace).
     if constexpr (L::kExtraRegs < L::kLaunchRegs) setmaxnreg_dec<L::kExtraRegs>();
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
     int stage = 0;
