@@ -312,6 +312,12 @@ def _load_traffic(name):
         return None
 
 
+def _hbm_bound(alg_bytes, flops, burst_tflops, hbm_gbs):
+    """True when a launch's algorithmic bytes at the measured copy bandwidth take
+    longer than its FLOPs at the measured dense bf16 peak."""
+    return alg_bytes / (hbm_gbs * 1e9) > flops / (burst_tflops * 1e12)
+
+
 def _roofline(hbm_bound, tflops, alg_bytes, ms, burst, sustained, hbm, src, traffic):
     """The binding roofline of the assignment launch: the tensor pipe when its
     FLOPs take longer at the measured GEMM peak than its algorithmic bytes at the
@@ -427,7 +433,7 @@ def run_ours(args, rank, world, local_rank):
     # the centroids read once, labels and float32 sums written once
     alg_bytes = sum(t.numel() * t.element_size() for t in (eng.x, eng.x_sq, eng.c_cur, eng.ids)
                     if t is not None) + eng.sums.numel() * 4
-    hbm_bound = alg_bytes / (hbm * 1e9) > flops_rank / (burst * 1e12)
+    hbm_bound = _hbm_bound(alg_bytes, flops_rank, burst, hbm)
 
     # ---- e2e through the public API with host buffers (each rank its batches)
     e2e = None
@@ -783,7 +789,7 @@ def run_assign(args, rank, world, local_rank):
     achieved = flops / (ms * 1e-3) / 1e12
     burst, sustained, hbm, src = _peaks()
     alg_bytes = sum(t.numel() * t.element_size() for t in (x, x_sq, c0, out))
-    hbm_bound = alg_bytes / (hbm * 1e9) > flops / (burst * 1e12)
+    hbm_bound = _hbm_bound(alg_bytes, flops, burst, hbm)
     if rank == 0:
         print(json.dumps({
             "metric": "assign TFLOP/s (euclid_assign_triton, labels only)",
