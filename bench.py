@@ -435,6 +435,37 @@ def run_ours(args, rank, world, local_rank):
                     if t is not None) + eng.sums.numel() * 4
     hbm_bound = _hbm_bound(alg_bytes, flops_rank, burst, hbm)
 
+    # ---- the labels-only assignment (`--op assign`'s kernel, the predict path)
+    # on the same resident data, so both assignment numbers come from one run
+    labels_only = None
+    if not sim:
+        from flash_kmeans.assign_euclid_triton import euclid_assign_triton
+        out_l = torch.empty((Bl, N), dtype=torch.int32, device=dev)
+        for _ in range(3):
+            euclid_assign_triton(eng.x, eng.c_cur, eng.x_sq, out=out_l)
+        n_l = max(steps, 5)
+        l0 = torch.cuda.Event(enable_timing=True)
+        l1 = torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        l0.record()
+        for _ in range(n_l):
+            euclid_assign_triton(eng.x, eng.c_cur, eng.x_sq, out=out_l)
+        l1.record()
+        torch.cuda.synchronize()
+        tl = torch.tensor([l0.elapsed_time(l1) / n_l], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tl, op=dist.ReduceOp.MAX)
+        lms = float(tl[0])
+        labels_only = {"ms": round(lms, 4),
+                       "tflops": round(flops_rank / (lms * 1e-3) / 1e12, 2),
+                       "frac_of_burst": round(flops_rank / (lms * 1e-3) / 1e12 / burst, 4),
+                       "calls": n_l,
+                       "call": "euclid_assign_triton(x, c, x_sq, out=...) on the engine's resident "
+                               "tensors, labels only (no sums), back to back"}
+        del out_l
+
     # ---- e2e through the public API with host buffers (each rank its batches)
     e2e = None
     if args.e2e_steps > 0:
@@ -515,6 +546,7 @@ def run_ours(args, rank, world, local_rank):
                        "step": "one Lloyd iteration incl. the per-iteration shift readback"},
             "ms_per_iter": round(ms, 4),
             "assign_ms": round(assign_ms, 4),
+            "assign_labels_only": labels_only,
             "roofline": _roofline(hbm_bound, achieved, alg_bytes, assign_ms, burst, sustained, hbm,
                                   src, None if sim else _load_traffic(args.workload)),
             "e2e": e2e,

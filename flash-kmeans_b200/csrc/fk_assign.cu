@@ -191,6 +191,8 @@ struct AssignParams {
   int total_tiles;
   int* status;
   int lo_b;         // 3xTF32 modes: the centroids' lo halves are batches lo_b.. of tmap_c
+  int xlo_b;        // 3xTF32 modes: 0 -> the converter warps split each x chunk; > 0 -> x
+                    // arrives split, its lo halves are batches xlo_b.. of tmap_x
 };
 
 __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
@@ -741,13 +743,20 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
                 break;
               }
               uint8_t* st = smem + L::stages_off + stage * L::stage_bytes;
-              mbar_arrive_expect_tx(&c_full[stage], kCChunk * L::kSplit + (XRES ? 0 : L::kXChunkL));
+              const int xparts = (split_mode(MODE) && p.xlo_b) ? 2 : 1;
+              mbar_arrive_expect_tx(&c_full[stage],
+                                    kCChunk * L::kSplit + (XRES ? 0 : L::kXChunkL * xparts));
               tma_load_3d(st + L::st_c, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent, b);
               if constexpr (split_mode(MODE))   // the centroids come split (hi, lo) per call
                 tma_load_3d(st + L::st_clo, &tmap_c, &c_full[stage], dc * p.dch, kt * kCent,
                             b + p.lo_b);
               if constexpr (!XRES)
                 tma_load_3d(st + L::st_x, &tmap_x, &c_full[stage], dc * p.dch, row0, b);
+              if constexpr (split_mode(MODE) && !XRES) {
+                if (p.xlo_b)   // x split once per fit: its lo half from the second half of tmap_x
+                  tma_load_3d(st + L::st_xlo, &tmap_x, &c_full[stage], dc * p.dch, row0,
+                              b + p.xlo_b);
+              }
               last_par[stage] = static_cast<int>(sph);
               if (++stage == STAGES) { stage = 0; sph ^= 1; }
             }
@@ -803,7 +812,7 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kCent);
           for (int dc = 0; dc < p.nd; ++dc) {
             const int sc = RESC ? kt * p.nd + dc : stage;
-            uint64_t* ready = split_mode(MODE) ? &conv_full[sc] : &c_full[sc];
+            uint64_t* ready = (split_mode(MODE) && !p.xlo_b) ? &conv_full[sc] : &c_full[sc];
             if (!RESC || new_batch) {
               if (!mbar_wait(ready, RESC ? static_cast<uint32_t>(bi & 1) : sph, abort_flag,
                              p.status, FK_DEV_WAIT_TIMEOUT)) {
@@ -1376,11 +1385,13 @@ __global__ void __launch_bounds__(Layout<MODE, XRES, STAGES, FUSE, EPI, KC, RESC
     // ------------------------------------- 3xTF32 split converters (modes 2, 4)
     // Each stage's x chunk is split in place into tf32 hi and the exact lo
     // rest (the centroid chunks arrive already split, from the workspace).
+    // With x split once per fit (p.xlo_b > 0) both halves arrive by TMA and
+    // these warps have nothing to do.
     if constexpr (L::kExtraRegs < L::kLaunchRegs) setmaxnreg_dec<L::kExtraRegs>();
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
     int stage = 0;
     uint32_t sph = 0;
-    bool ok = true;
+    bool ok = p.xlo_b == 0;
     for (int t = t_begin; ok && t < t_end; ++t) {
       for (int kt = 0; ok && kt < p.nkt; ++kt) {
         for (int dc = 0; dc < p.nd; ++dc) {
@@ -1591,7 +1602,7 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
                         int64_t N, int64_t K, int64_t D, const int64_t* xs, const int64_t* cs,
                         const int64_t* xqs, const int64_t* cqs, const int64_t* os, void* ws,
                         int32_t* status, cudaStream_t stream, float* sums = nullptr,
-                        bool dot = false) {
+                        bool dot = false, bool xsplit = false) {
   constexpr int eb = Elem<T>::kBytes;
   const bool is16 = eb == 2;
   const int mode = dot ? (is16 ? 3 : 4) : (is16 ? (xsq_dtype == Elem<T>::kDtype ? 0 : 1) : 2);
@@ -1683,7 +1694,9 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
 
   // 2) tensor maps: x as (D, N, B), centroids (or -2c) as (D, K, B), 128-byte swizzle
   CUtensorMap tx, tc;
-  int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, B, xs[1] * eb, xs[0] * eb, dch, kRows, w64);
+  // (x split once per fit: its hi halves are batches [0, B), the lo halves [B, 2B))
+  int st = encode_tmap_3d(&tx, x, Elem<T>::kDtype, D, N, xsplit ? 2 * B : B, xs[1] * eb, xs[0] * eb,
+                          dch, kRows, w64);
   if (st != FK_OK) return st;
   if (cneg)
     st = encode_tmap_3d(&tc, cneg, Elem<T>::kDtype, D, K, B, dp * eb, K * dp * eb, dch, kc);
@@ -1716,6 +1729,7 @@ static int assign_typed(const void* x, const void* cent, const void* x_sq, const
   p.total_tiles = static_cast<int>(B * p.ntn);
   p.status = status;
   p.lo_b = static_cast<int>(B);
+  p.xlo_b = xsplit ? static_cast<int>(B) : 0;
 
   if (dot) {
     if constexpr (Elem<T>::kBytes == 2) {
@@ -1784,7 +1798,7 @@ static int assign_entry(const char* fn, bool dot, const void* x, const void* cen
                         int64_t D, const int64_t* x_strides3, const int64_t* c_strides3,
                         const int64_t* xsq_strides2, const int64_t* csq_strides2,
                         const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
-                        int32_t* dev_status, void* stream) {
+                        int32_t* dev_status, void* stream, bool xsplit = false) {
   if (B < 0 || N < 0 || K <= 0 || D <= 0)
     return fail(FK_ERR_INVALID_ARG, "%s: bad sizes B=%lld N=%lld K=%lld D=%lld", fn,
                 (long long)B, (long long)N, (long long)K, (long long)D);
@@ -1834,7 +1848,7 @@ static int assign_entry(const char* fn, bool dot, const void* x, const void* cen
     default:
       return assign_typed<float>(x, centroids, x_sq, c_sq, out, counts, xsq_dtype, csq_dtype, B, N,
                                  K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2,
-                                 out_strides2, workspace, dev_status, s, nullptr, dot);
+                                 out_strides2, workspace, dev_status, s, nullptr, dot, xsplit);
   }
 }
 
@@ -1897,12 +1911,25 @@ static bool assign_accumulate_priv(int64_t K, int64_t D, int dtype) {
 }
 
 extern "C" int fk_assign_accumulate_method(int64_t K, int64_t D, int dtype) {
+  if (dtype == FK_F32_XSPLIT) dtype = FK_F32;
   if (assign_accumulate_fused(K, D, dtype)) return FK_ACC_FUSED;
   return assign_accumulate_priv(K, D, dtype) ? FK_ACC_PRIVATISED : FK_ACC_SORTED;
 }
 
+// FK_F32_XSPLIT: x's tf32 hi halves and exact rests, (2B, N, Dx) float32 with
+// Dx = D rounded up to 4 (16-byte rows for TMA), after FK_F32's workspace.
+static int64_t xsplit_row(int64_t D) { return (D + 3) / 4 * 4; }
+
+static size_t xsplit_offset(int64_t B, int64_t N, int64_t K, int64_t D) {
+  return align_up(fk_assign_accumulate_workspace_size(B, N, K, D, FK_F32), 256);
+}
+
 extern "C" size_t fk_assign_accumulate_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                       int dtype) {
+  if (dtype == FK_F32_XSPLIT) {
+    const size_t rows = (B > 0 && N > 0) ? static_cast<size_t>(2 * B * N) : 0;
+    return xsplit_offset(B, N, K, D) + align_up(rows * xsplit_row(D > 0 ? D : 1) * 4, 256);
+  }
   const size_t wa = fk_assign_workspace_size(B, K, D, dtype);
   if (assign_accumulate_priv(K, D, dtype) || assign_accumulate_fused(K, D, dtype)) return wa;
   return wa + align_up(static_cast<size_t>(B > 0 && K > 0 ? B * K : 1) * 4, 256) +
@@ -1927,10 +1954,24 @@ static int assign_accumulate_entry(const char* fn, bool dot, const void* x, cons
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(FK_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-aligned", fn, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // FK_F32_XSPLIT: the assignment reads x's halves from the workspace, the
+  // sums read x itself
+  const bool xsplit = dtype == FK_F32_XSPLIT;
+  if (xsplit) dtype = FK_F32;
+  const void* xa = x;
+  const int64_t* xa_strides = x_strides3;
+  int64_t xs_split[3] = {0, 0, 1};
+  if (xsplit) {
+    const int64_t dx = xsplit_row(D);
+    xs_split[0] = N * dx;
+    xs_split[1] = dx;
+    xa = static_cast<uint8_t*>(workspace) + xsplit_offset(B, N, K, D);
+    xa_strides = xs_split;
+  }
   auto assign = [&](int32_t* cnt, size_t ws_bytes) {
-    return assign_entry(fn, dot, x, centroids, x_sq, c_sq, out, cnt, dtype, xsq_dtype, csq_dtype, B,
-                        N, K, D, x_strides3, c_strides3, xsq_strides2, csq_strides2, out_strides2,
-                        workspace, ws_bytes, dev_status, stream);
+    return assign_entry(fn, dot, xa, centroids, x_sq, c_sq, out, cnt, dtype, xsq_dtype, csq_dtype,
+                        B, N, K, D, xa_strides, c_strides3, xsq_strides2, csq_strides2,
+                        out_strides2, workspace, ws_bytes, dev_status, stream, xsplit);
   };
   if (assign_accumulate_priv(K, D, dtype)) {
     int st = assign(nullptr, workspace_bytes);
@@ -2007,6 +2048,68 @@ extern "C" int fk_assign_dot_accumulate(const void* x, const void* centroids, in
                                  out, counts, sums, dtype, FK_F32, FK_F32, B, N, K, D, x_strides3,
                                  c_strides3, nullptr, nullptr, out_strides2, workspace,
                                  workspace_bytes, dev_status, stream);
+}
+
+// ---------------------------------------------------------------------------
+// fk_assign_accumulate_split_x: x's tf32 hi halves and exact rests, once per
+// fit, into the FK_F32_XSPLIT workspace (hi = the split_centroids_kernel rule).
+// ---------------------------------------------------------------------------
+namespace fk {
+__device__ __forceinline__ float tf32_hi(float v) {
+  return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
+}
+
+// dense x (rows of D % 4 == 0 floats back to back): four floats per thread step
+__global__ void split_rows_flat_kernel(const float4* __restrict__ x, float4* __restrict__ out,
+                                       int64_t n4) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = __ldcs(x + i);
+    float4 h, l;
+    h.x = tf32_hi(v.x); l.x = v.x - h.x;
+    h.y = tf32_hi(v.y); l.y = v.y - h.y;
+    h.z = tf32_hi(v.z); l.z = v.z - h.z;
+    h.w = tf32_hi(v.w); l.w = v.w - h.w;
+    __stcs(out + i, h);
+    __stcs(out + n4 + i, l);
+  }
+}
+}  // namespace fk
+
+extern "C" int fk_assign_accumulate_split_x(const float* x, int64_t B, int64_t N, int64_t K,
+                                            int64_t D, const int64_t* x_strides3, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  if (B < 0 || N < 0 || K <= 0 || D <= 0)
+    return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate_split_x: bad sizes");
+  if (B == 0 || N == 0) return FK_OK;
+  if (!x || !x_strides3) return fail(FK_ERR_INVALID_ARG, "fk_assign_accumulate_split_x: null x");
+  if (N >= (1ll << 31)) return fail(FK_ERR_UNSUPPORTED, "fk_assign_accumulate_split_x: N >= 2^31");
+  const size_t need = fk_assign_accumulate_workspace_size(B, N, K, D, FK_F32_XSPLIT);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FK_ERR_WORKSPACE, "fk_assign_accumulate_split_x: workspace needs %zu bytes, 256-aligned",
+                need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* out = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + xsplit_offset(B, N, K, D));
+  const int64_t dx = xsplit_row(D);
+  const int64_t xs0 = B == 1 ? N * x_strides3[1] : x_strides3[0];
+  const bool dense = D == dx && x_strides3[2] == 1 && (N == 1 || x_strides3[1] == D) &&
+                     xs0 == N * D && reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  const int sms = sm_count_current();
+  const int64_t cap = sms > 0 ? static_cast<int64_t>(sms) * 8 : 1024;
+  if (dense) {
+    const int64_t n4 = B * N * D / 4;
+    const int blocks = static_cast<int>((n4 + 255) / 256 < cap ? (n4 + 255) / 256 : cap);
+    split_rows_flat_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x),
+                                                  reinterpret_cast<float4*>(out), n4);
+    return check_launch("split_rows_flat_kernel");
+  }
+  // any strides: one element per thread step, zeros in columns [D, Dx)
+  const int64_t total = B * N * dx;
+  const int blocks = static_cast<int>((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
+  split_centroids_kernel<<<blocks, 256, 0, s>>>(x, xs0, N == 1 ? dx : x_strides3[1], x_strides3[2],
+                                                out, dx, static_cast<int>(N), static_cast<int>(D),
+                                                total, total);
+  return check_launch("split_centroids_kernel");
 }
 
 // ---------------------------------------------------------------------------

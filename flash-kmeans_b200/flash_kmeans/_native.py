@@ -16,6 +16,7 @@ LIB_NAME = "libflashkmeans_b200.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", LIB_NAME)
 
 FK_F16, FK_BF16, FK_F32, FK_I32, FK_I64 = 0, 1, 2, 3, 4
+FK_F32_XSPLIT = 5   # float32 x split once into tf32 halves (the *_accumulate entry points)
 FK_ACC_PRIVATISED, FK_ACC_FUSED, FK_ACC_SORTED = 0, 1, 2  # fk_assign_accumulate_method
 FK_OK = 0
 FK_DEV_BAD_LABEL = 101
@@ -55,6 +56,7 @@ SIGNATURES = {
     "fk_assign_accumulate_method": (_I, [_L, _L, _I]),
     "fk_assign_accumulate": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL, _PL,
                                   _PL, _PL, _PL, _P, _S, _P, _P]),
+    "fk_assign_accumulate_split_x": (_I, [_P, _L, _L, _L, _L, _PL, _P, _S, _P]),
     "fk_assign_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _PL,
                                       _PL, _PL, _PL, _PL, _P, _P]),
     "fk_centroid_accumulate_workspace_size": (_S, [_L, _L, _L]),

@@ -77,7 +77,16 @@ class LloydEngine:
         self._stat_k = [-1, -1]   # iteration whose record each slot holds
         self.csq_valid = False
         lib = nat.load()
-        ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.dtype_code(dtype))
+        # float32 x: its tf32 halves are split once per load() into the
+        # workspace (twice x's bytes) when the device has room, instead of in
+        # every assignment tile
+        self.xcode = nat.dtype_code(dtype)
+        ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, self.xcode)
+        if dtype == torch.float32:
+            split_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.FK_F32_XSPLIT)
+            free, _ = torch.cuda.mem_get_info(dev)
+            if split_bytes - ws_bytes < free // 2:
+                self.xcode, ws_bytes = nat.FK_F32_XSPLIT, split_bytes
         self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None
@@ -125,6 +134,12 @@ class LloydEngine:
         self.x = _ops.ensure_tma(x)
         if self.metric == "euclid":
             self.x_sq = x_sq if x_sq is not None else _ops.row_sqnorm(self.x)
+        if self.xcode == nat.FK_F32_XSPLIT:
+            with torch.cuda.device(self.device):
+                nat.check(nat.load().fk_assign_accumulate_split_x(
+                    nat.ptr(self.x), self.B, self.N, self.K, self.D, nat.strides(self.x, 3),
+                    nat.ptr(self.ws), self.ws.numel(), nat.stream_handle(self.device)),
+                    "fk_assign_accumulate_split_x")
         self._k = 0
         self._stat_k = [-1, -1]
         self.c_cur.copy_(centroids.view(self.B, self.K, self.D))
@@ -213,13 +228,13 @@ class LloydEngine:
         status = nat.ptr(self.stat[1:2])
         if which == "assign" and self.metric == "dot":
             a = (nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.ids), nat.ptr(self.hist),
-                 nat.ptr(self.sums), nat.dtype_code(x.dtype), B, N, K, D, nat.strides(x, 3),
+                 nat.ptr(self.sums), self.xcode, B, N, K, D, nat.strides(x, 3),
                  nat.strides(self.c_cur, 3), nat.strides(self.ids, 2), nat.ptr(self.ws),
                  self.ws.numel(), status)
         elif which == "assign":
             a = (nat.ptr(x), nat.ptr(self.c_cur), nat.ptr(self.x_sq),
                  nat.ptr(self.csq if c_sq_on else None), nat.ptr(self.ids), nat.ptr(self.hist),
-                 nat.ptr(self.sums), nat.dtype_code(x.dtype), nat.dtype_code(self.x_sq.dtype),
+                 nat.ptr(self.sums), self.xcode, nat.dtype_code(self.x_sq.dtype),
                  nat.FK_F32, B, N, K, D, nat.strides(x, 3), nat.strides(self.c_cur, 3),
                  nat.strides(self.x_sq, 2), nat.strides(self.csq, 2), nat.strides(self.ids, 2),
                  nat.ptr(self.ws), self.ws.numel(), status)

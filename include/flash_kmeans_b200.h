@@ -60,8 +60,10 @@ extern "C" {
 
 #define FK_ABI_VERSION 2
 
-/* element types */
-enum fk_dtype { FK_F16 = 0, FK_BF16 = 1, FK_F32 = 2, FK_I32 = 3, FK_I64 = 4 };
+/* element types.  FK_F32_XSPLIT is accepted by the *_accumulate entry points
+ * only: float32 x whose tf32 hi halves and exact rests the workspace holds,
+ * split once by fk_assign_accumulate_split_x (see there). */
+enum fk_dtype { FK_F16 = 0, FK_BF16 = 1, FK_F32 = 2, FK_I32 = 3, FK_I64 = 4, FK_F32_XSPLIT = 5 };
 
 /* host-side status codes */
 enum fk_status {
@@ -181,6 +183,21 @@ int fk_assign_dot_accumulate(const void* x, const void* centroids, int32_t* out,
                              const int64_t* x_strides3, const int64_t* c_strides3,
                              const int64_t* out_strides2, void* workspace, size_t workspace_bytes,
                              int32_t* dev_status, void* stream);
+
+/* Float32 x split once for many Lloyd iterations (no counterpart in the
+ * reference, whose float32 assignment is plain TF32).  The 3xTF32 assignment
+ * needs x as tf32 hi = x rounded to 10 explicit mantissa bits and the exact
+ * rest lo = x - hi; fk_assign_accumulate / fk_assign_dot_accumulate split each
+ * x tile in shared memory on every call.  With dtype FK_F32_XSPLIT they
+ * instead load both halves from the workspace (x itself still feeds the
+ * centroid sums), which this call fills from x: a (2B, N, Dx) float32 array,
+ * Dx = D rounded up to 4, at the end of a workspace of
+ * fk_assign_accumulate_workspace_size(B, N, K, D, FK_F32_XSPLIT) bytes
+ * (2*B*N*Dx*4 bytes more than FK_F32's).  Call it again whenever x changes;
+ * labels, sums and counts are the same as with FK_F32. */
+int fk_assign_accumulate_split_x(const float* x, int64_t B, int64_t N, int64_t K, int64_t D,
+                                 const int64_t* x_strides3, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* fk_assign for callers that cannot allocate (no counterpart in the reference).
  * Some hosts give a plugin only its inputs and outputs: a serving framework's

@@ -115,3 +115,25 @@ def test_accumulate_method_codes_are_stable(lib):
     assert lib.fk_assign_accumulate_method(128, 128, 2) == _native.FK_ACC_PRIVATISED
     assert lib.fk_assign_accumulate_method(1000, 128, 0) == _native.FK_ACC_FUSED
     assert lib.fk_assign_accumulate_method(1024, 2048, 2) == _native.FK_ACC_SORTED
+
+
+def test_xsplit_workspace_and_validation(lib):
+    """FK_F32_XSPLIT: FK_F32's accumulate workspace plus x's (2B, N, Dx) float32
+    halves (Dx = D rounded up to 4), the same method as FK_F32, and host-side
+    argument checks of fk_assign_accumulate_split_x (no launch)."""
+    from flash_kmeans import _native
+    X = _native.FK_F32_XSPLIT
+    for B, N, K, D in [(1, 262144, 1024, 2048), (3, 333, 70, 37), (2, 1000, 300, 128)]:
+        base = lib.fk_assign_accumulate_workspace_size(B, N, K, D, 2)
+        dx = (D + 3) // 4 * 4
+        got = lib.fk_assign_accumulate_workspace_size(B, N, K, D, X)
+        assert got >= base + 2 * B * N * dx * 4
+        assert got < base + 2 * B * N * dx * 4 + 1024
+        assert lib.fk_assign_accumulate_method(K, D, X) == lib.fk_assign_accumulate_method(K, D, 2)
+    st3 = (ctypes.c_int64 * 3)(1000 * 128, 128, 1)
+    p = ctypes.c_void_p(1 << 20)
+    small = lib.fk_assign_accumulate_workspace_size(2, 1000, 300, 128, 2)
+    assert lib.fk_assign_accumulate_split_x(None, 2, 1000, 300, 128, st3, p, 1 << 30, None) == 1
+    assert lib.fk_assign_accumulate_split_x(p, 2, 1000, 0, 128, st3, p, 1 << 30, None) == 1
+    assert lib.fk_assign_accumulate_split_x(p, 2, 1000, 300, 128, st3, p, small, None) == 3
+    assert lib.fk_assign_accumulate_split_x(p, 0, 1000, 300, 128, st3, None, 0, None) == 0

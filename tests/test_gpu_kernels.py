@@ -310,3 +310,69 @@ def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     assert torch.equal(out, ref)
     assert torch.equal(cnts, ref_c)
     torch.testing.assert_close(sums, ref_s, rtol=1e-5, atol=1e-3)
+
+
+# ------------------------------------------- float32 x split once (FK_F32_XSPLIT)
+@pytest.mark.parametrize("metric", ["euclid", "dot"])
+@pytest.mark.parametrize("B,N,K,D,layout", [
+    (2, 1000, 300, 128, "dense"),      # 128-byte chunk rows, two stages
+    (1, 700, 260, 640, "dense"),       # 64-byte chunk rows, four stages (D >= 512)
+    (3, 333, 70, 37, "padded"),        # rows padded to 40 floats: the strided split
+    (2, 500, 40, 48, "strided")])      # a non-contiguous view of x
+def test_xsplit_matches_tile_split(fk, metric, B, N, K, D, layout):
+    """fk_assign_accumulate / fk_assign_dot_accumulate with x split once per fit
+    into the workspace (FK_F32_XSPLIT) give the same labels, counts and sums,
+    bit for bit, as with each x tile split in shared memory (FK_F32): both use
+    the same tf32 hi/lo halves and the same MMA order."""
+    from flash_kmeans import _native as nat
+    from flash_kmeans import _ops
+    lib = nat.load()
+    rng = np.random.default_rng(B * 31 + D + K)
+    xa = rng.standard_normal((B, N, D), dtype=np.float32)
+    if layout == "strided":
+        big = torch.from_numpy(rng.standard_normal((B, N, 2 * D), dtype=np.float32)).cuda()
+        big[..., ::2] = torch.from_numpy(xa).cuda()
+        x = big[..., ::2]
+        xt = _ops.ensure_tma(x.contiguous())
+    else:
+        xt = _ops.ensure_tma(torch.from_numpy(xa).cuda())
+        x = xt
+    c = _ops.ensure_tma(torch.from_numpy(rng.standard_normal((B, K, D), dtype=np.float32)).cuda())
+    xsq = _ops.row_sqnorm(xt) if metric == "euclid" else None
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+
+    def run(code):
+        out = torch.full((B, N), -1, dtype=torch.int32, device="cuda")
+        sums = torch.zeros((B, K, D), device="cuda")
+        cnts = torch.zeros((B, K), dtype=torch.int32, device="cuda")
+        ws = torch.empty(lib.fk_assign_accumulate_workspace_size(B, N, K, D, code),
+                         dtype=torch.uint8, device="cuda")
+        s = nat.stream_handle(xt.device)
+        if code == nat.FK_F32_XSPLIT:
+            # the split reads x through its own strides (strided case: the view)
+            nat.check(lib.fk_assign_accumulate_split_x(nat.ptr(x), B, N, K, D, nat.strides(x, 3),
+                                                       nat.ptr(ws), ws.numel(), s),
+                      "fk_assign_accumulate_split_x")
+        if metric == "euclid":
+            nat.check(lib.fk_assign_accumulate(
+                nat.ptr(xt), nat.ptr(c), nat.ptr(xsq), None, nat.ptr(out), nat.ptr(cnts),
+                nat.ptr(sums), code, nat.dtype_code(xsq.dtype), 0, B, N, K, D,
+                nat.strides(xt, 3), nat.strides(c, 3), nat.strides(xsq, 2), None,
+                nat.strides(out, 2), nat.ptr(ws), ws.numel(), nat.ptr(status), s),
+                "fk_assign_accumulate")
+        else:
+            nat.check(lib.fk_assign_dot_accumulate(
+                nat.ptr(xt), nat.ptr(c), nat.ptr(out), nat.ptr(cnts), nat.ptr(sums), code,
+                B, N, K, D, nat.strides(xt, 3), nat.strides(c, 3), nat.strides(out, 2),
+                nat.ptr(ws), ws.numel(), nat.ptr(status), s), "fk_assign_dot_accumulate")
+        torch.cuda.synchronize()
+        assert int(status[0]) == 0
+        return out, cnts, sums
+
+    o1, c1, s1 = run(nat.FK_F32)
+    o2, c2, s2 = run(nat.FK_F32_XSPLIT)
+    assert int((o1 < 0).sum()) == 0
+    assert torch.equal(o1, o2)
+    assert torch.equal(c1, c2)
+    ref_s, _ = _torch_sums(xt, o1, K)
+    torch.testing.assert_close(s2, ref_s, rtol=1e-5, atol=1e-3)
