@@ -21,7 +21,10 @@ B200 design:
   share the host's PCIe bandwidth);
 * x_sq per block is computed once and kept on the device;
 * each block goes through fk_assign_accumulate: labels, counts and per-cluster
-  row sums in one call (one kernel for 16-bit data with D <= 128);
+  row sums in one call (one kernel for 16-bit data with D <= 128); float32
+  blocks are first split into their tf32 halves (fk_assign_accumulate_split_x,
+  one HBM pass) so the 3xTF32 assignment loads them instead of splitting
+  every tile in shared memory;
 * reduction: every device ends with identical sums/counts after an NCCL
   all-reduce (single-process communicator over the devices, or the process
   group when one process drives one GPU), then finalizes its own replica, so
@@ -120,9 +123,17 @@ class _DeviceLane:
             self.stat_host = torch.empty(4, dtype=torch.int32, pin_memory=True)
             self.csq_valid = False
             lib = nat.load()
-            self.ws = torch.empty(
-                lib.fk_assign_accumulate_workspace_size(B, nb, K, D, nat.dtype_code(dtype)),
-                dtype=torch.uint8, device=dev)
+            # float32 blocks: x's tf32 halves are split once per block and pass
+            # into the workspace (FK_F32_XSPLIT) instead of in every assignment
+            # tile, when the halves take at most a quarter of the free memory
+            self.xcode = nat.dtype_code(dtype)
+            ws_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, self.xcode)
+            if dtype == torch.float32:
+                split_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, nat.FK_F32_XSPLIT)
+                free, _ = torch.cuda.mem_get_info(dev)
+                if split_bytes - ws_bytes <= free // 4:
+                    self.xcode, ws_bytes = nat.FK_F32_XSPLIT, split_bytes
+            self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         # Copies form one sequence over passes: element s streams block s % nb
         # into buffer slot s % 2, so consecutive copies always alternate slots.
         self._issued = 0
@@ -224,8 +235,12 @@ class _DeviceLane:
                     nat.check(lib.fk_assign(*args, None, nat.dtype_code(xb.dtype), *tail),
                               "fk_assign")
                 else:  # labels, counts and row sums of this block in one pass
+                    if self.xcode == nat.FK_F32_XSPLIT:
+                        nat.check(lib.fk_assign_accumulate_split_x(
+                            nat.ptr(xb), B, nb, K, D, nat.strides(xb, 3), nat.ptr(self.ws),
+                            self.ws.numel(), s), "fk_assign_accumulate_split_x")
                     nat.check(lib.fk_assign_accumulate(*args, nat.ptr(self.cnt), nat.ptr(self.sums),
-                                                       nat.dtype_code(xb.dtype), *tail),
+                                                       self.xcode, *tail),
                               "fk_assign_accumulate")
                 if not self.resident:
                     self.free[slot].record(ks)
