@@ -17,6 +17,10 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", LIB_
 
 FK_F16, FK_BF16, FK_F32, FK_I32, FK_I64 = 0, 1, 2, 3, 4
 FK_F32_XSPLIT = 5   # float32 x split once into tf32 halves (the *_accumulate entry points)
+# Widest rows for which the drivers use FK_F32_XSPLIT: measured 11 % faster at
+# D = 128 and 256, 4 % at 512, no faster at 2048 (there the stages are fed from
+# L2 and the extra TMA load costs what the shared-memory split did)
+XSPLIT_MAX_D = 512
 FK_ACC_PRIVATISED, FK_ACC_FUSED, FK_ACC_SORTED = 0, 1, 2  # fk_assign_accumulate_method
 FK_OK = 0
 FK_DEV_BAD_LABEL = 101

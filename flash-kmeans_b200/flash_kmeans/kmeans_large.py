@@ -22,9 +22,9 @@ B200 design:
 * x_sq per block is computed once and kept on the device;
 * each block goes through fk_assign_accumulate: labels, counts and per-cluster
   row sums in one call (one kernel for 16-bit data with D <= 128); float32
-  blocks are first split into their tf32 halves (fk_assign_accumulate_split_x,
-  one HBM pass) so the 3xTF32 assignment loads them instead of splitting
-  every tile in shared memory;
+  blocks of rows up to XSPLIT_MAX_D floats are first split into their tf32
+  halves (fk_assign_accumulate_split_x, one HBM pass) so the 3xTF32
+  assignment loads them instead of splitting every tile in shared memory;
 * reduction: every device ends with identical sums/counts after an NCCL
   all-reduce (single-process communicator over the devices, or the process
   group when one process drives one GPU), then finalizes its own replica, so
@@ -123,12 +123,13 @@ class _DeviceLane:
             self.stat_host = torch.empty(4, dtype=torch.int32, pin_memory=True)
             self.csq_valid = False
             lib = nat.load()
-            # float32 blocks: x's tf32 halves are split once per block and pass
-            # into the workspace (FK_F32_XSPLIT) instead of in every assignment
-            # tile, when the halves take at most a quarter of the free memory
+            # float32 blocks with rows of at most XSPLIT_MAX_D: x's tf32 halves
+            # are split once per block and pass into the workspace
+            # (FK_F32_XSPLIT) instead of in every assignment tile, when the
+            # halves take at most a quarter of the free memory
             self.xcode = nat.dtype_code(dtype)
             ws_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, self.xcode)
-            if dtype == torch.float32:
+            if dtype == torch.float32 and D <= nat.XSPLIT_MAX_D:
                 split_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, nat.FK_F32_XSPLIT)
                 free, _ = torch.cuda.mem_get_info(dev)
                 if split_bytes - ws_bytes <= free // 4:

@@ -77,12 +77,12 @@ class LloydEngine:
         self._stat_k = [-1, -1]   # iteration whose record each slot holds
         self.csq_valid = False
         lib = nat.load()
-        # float32 x: its tf32 halves are split once per load() into the
-        # workspace (twice x's bytes) when the device has room, instead of in
-        # every assignment tile
+        # float32 x with rows of at most XSPLIT_MAX_D: its tf32 halves are
+        # split once per load() into the workspace (twice x's bytes) when the
+        # device has room, instead of in every assignment tile
         self.xcode = nat.dtype_code(dtype)
         ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, self.xcode)
-        if dtype == torch.float32:
+        if dtype == torch.float32 and D <= nat.XSPLIT_MAX_D:
             split_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.FK_F32_XSPLIT)
             free, _ = torch.cuda.mem_get_info(dev)
             if split_bytes - ws_bytes < free // 2:
