@@ -2074,6 +2074,31 @@ __global__ void split_rows_flat_kernel(const float4* __restrict__ x, float4* __r
     __stcs(out + n4 + i, l);
   }
 }
+// rows with their own batch and row strides (unit column stride, D % 4 == 0,
+// 16-byte aligned rows, e.g. one block of a larger buffer): one warp per row
+// step, so the row's batch and index cost one division per row, not per element
+__global__ void split_rows_vec_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxn,
+                                      float4* __restrict__ out, int N, int d4, int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t lo_off = rows * d4;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += nw) {
+    const int64_t b = r / N;
+    const float4* src = reinterpret_cast<const float4*>(x + b * sxb + (r - b * N) * sxn);
+    float4* dst = out + r * d4;
+    for (int j = lane; j < d4; j += 32) {
+      const float4 v = __ldcs(src + j);
+      float4 h, l;
+      h.x = tf32_hi(v.x); l.x = v.x - h.x;
+      h.y = tf32_hi(v.y); l.y = v.y - h.y;
+      h.z = tf32_hi(v.z); l.z = v.z - h.z;
+      h.w = tf32_hi(v.w); l.w = v.w - h.w;
+      __stcs(dst + j, h);
+      __stcs(dst + lo_off + j, l);
+    }
+  }
+}
 }  // namespace fk
 
 extern "C" int fk_assign_accumulate_split_x(const float* x, int64_t B, int64_t N, int64_t K,
@@ -2102,6 +2127,15 @@ extern "C" int fk_assign_accumulate_split_x(const float* x, int64_t B, int64_t N
     split_rows_flat_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x),
                                                   reinterpret_cast<float4*>(out), n4);
     return check_launch("split_rows_flat_kernel");
+  }
+  if (D == dx && x_strides3[2] == 1 && xs0 % 4 == 0 && (N == 1 || x_strides3[1] % 4 == 0) &&
+      reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    const int64_t rows = B * N;   // eight rows per 256-thread block step
+    const int blocks = static_cast<int>((rows + 7) / 8 < cap ? (rows + 7) / 8 : cap);
+    split_rows_vec_kernel<<<blocks, 256, 0, s>>>(x, xs0, N == 1 ? 0 : x_strides3[1],
+                                                 reinterpret_cast<float4*>(out), static_cast<int>(N),
+                                                 static_cast<int>(D / 4), rows);
+    return check_launch("split_rows_vec_kernel");
   }
   // any strides: one element per thread step, zeros in columns [D, Dx)
   const int64_t total = B * N * dx;

@@ -318,7 +318,8 @@ def test_assign_accumulate_matches_separate_path(fk, dt, B, N, K, D):
     (2, 1000, 300, 128, "dense"),      # 128-byte chunk rows, two stages
     (1, 700, 260, 640, "dense"),       # 64-byte chunk rows, four stages (D >= 512)
     (3, 333, 70, 37, "padded"),        # rows padded to 40 floats: the strided split
-    (2, 500, 40, 48, "strided")])      # a non-contiguous view of x
+    (2, 500, 40, 48, "strided"),       # a non-contiguous view of x (every other column)
+    (3, 700, 90, 128, "rowview")])     # rows 0..N-1 of a longer buffer: the row-wise split
 def test_xsplit_matches_tile_split(fk, metric, B, N, K, D, layout):
     """fk_assign_accumulate / fk_assign_dot_accumulate with x split once per fit
     into the workspace (FK_F32_XSPLIT) give the same labels, counts and sums,
@@ -333,6 +334,11 @@ def test_xsplit_matches_tile_split(fk, metric, B, N, K, D, layout):
         big = torch.from_numpy(rng.standard_normal((B, N, 2 * D), dtype=np.float32)).cuda()
         big[..., ::2] = torch.from_numpy(xa).cuda()
         x = big[..., ::2]
+        xt = _ops.ensure_tma(x.contiguous())
+    elif layout == "rowview":
+        big = torch.from_numpy(rng.standard_normal((B, N + 13, D), dtype=np.float32)).cuda()
+        big[:, :N] = torch.from_numpy(xa).cuda()
+        x = big[:, :N]
         xt = _ops.ensure_tma(x.contiguous())
     else:
         xt = _ops.ensure_tma(torch.from_numpy(xa).cuda())
