@@ -21,6 +21,21 @@ FK_F32_XSPLIT = 5   # float32 x split once into tf32 halves (the *_accumulate en
 # D = 128 and 256, 4 % at 512, no faster at 2048 (there the stages are fed from
 # L2 and the extra TMA load costs what the shared-memory split did)
 XSPLIT_MAX_D = 512
+
+
+def accumulate_x_code(lib, dtype, B: int, N: int, K: int, D: int, free_bytes: int,
+                      share: float) -> tuple:
+    """(dtype code, workspace bytes) for fk_assign_accumulate: FK_F32_XSPLIT
+    for float32 rows of at most XSPLIT_MAX_D elements when its extra workspace
+    (x's two tf32 halves) takes at most `share` of `free_bytes`, else the
+    plain code of `dtype`."""
+    code = dtype_code(dtype)
+    ws = lib.fk_assign_accumulate_workspace_size(B, N, K, D, code)
+    if code == FK_F32 and D <= XSPLIT_MAX_D:
+        split = lib.fk_assign_accumulate_workspace_size(B, N, K, D, FK_F32_XSPLIT)
+        if split - ws <= free_bytes * share:
+            return FK_F32_XSPLIT, split
+    return code, ws
 FK_ACC_PRIVATISED, FK_ACC_FUSED, FK_ACC_SORTED = 0, 1, 2  # fk_assign_accumulate_method
 FK_OK = 0
 FK_DEV_BAD_LABEL = 101

@@ -127,13 +127,8 @@ class _DeviceLane:
             # are split once per block and pass into the workspace
             # (FK_F32_XSPLIT) instead of in every assignment tile, when the
             # halves take at most a quarter of the free memory
-            self.xcode = nat.dtype_code(dtype)
-            ws_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, self.xcode)
-            if dtype == torch.float32 and D <= nat.XSPLIT_MAX_D:
-                split_bytes = lib.fk_assign_accumulate_workspace_size(B, nb, K, D, nat.FK_F32_XSPLIT)
-                free, _ = torch.cuda.mem_get_info(dev)
-                if split_bytes - ws_bytes <= free // 4:
-                    self.xcode, ws_bytes = nat.FK_F32_XSPLIT, split_bytes
+            free = torch.cuda.mem_get_info(dev)[0] if dtype == torch.float32 else 0
+            self.xcode, ws_bytes = nat.accumulate_x_code(lib, dtype, B, nb, K, D, free, 0.25)
             self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         # Copies form one sequence over passes: element s streams block s % nb
         # into buffer slot s % 2, so consecutive copies always alternate slots.

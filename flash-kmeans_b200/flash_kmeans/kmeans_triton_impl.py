@@ -80,13 +80,8 @@ class LloydEngine:
         # float32 x with rows of at most XSPLIT_MAX_D: its tf32 halves are
         # split once per load() into the workspace (twice x's bytes) when the
         # device has room, instead of in every assignment tile
-        self.xcode = nat.dtype_code(dtype)
-        ws_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, self.xcode)
-        if dtype == torch.float32 and D <= nat.XSPLIT_MAX_D:
-            split_bytes = lib.fk_assign_accumulate_workspace_size(B, N, K, D, nat.FK_F32_XSPLIT)
-            free, _ = torch.cuda.mem_get_info(dev)
-            if split_bytes - ws_bytes < free // 2:
-                self.xcode, ws_bytes = nat.FK_F32_XSPLIT, split_bytes
+        free = torch.cuda.mem_get_info(dev)[0] if dtype == torch.float32 else 0
+        self.xcode, ws_bytes = nat.accumulate_x_code(lib, dtype, B, N, K, D, free, 0.5)
         self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         self.x = None
         self.x_sq = None

@@ -137,3 +137,24 @@ def test_xsplit_workspace_and_validation(lib):
     assert lib.fk_assign_accumulate_split_x(p, 2, 1000, 0, 128, st3, p, 1 << 30, None) == 1
     assert lib.fk_assign_accumulate_split_x(p, 2, 1000, 300, 128, st3, p, small, None) == 3
     assert lib.fk_assign_accumulate_split_x(p, 0, 1000, 300, 128, st3, None, 0, None) == 0
+
+
+def test_split_x_choice(lib):
+    """The drivers' choice of the split-x form: float32 rows of at most
+    XSPLIT_MAX_D elements, and only when x's halves fit the given share of the
+    free device memory; 16-bit x and wider rows keep their plain code."""
+    import torch
+    from flash_kmeans import _native
+    B, N, K, D = 1, 1 << 20, 8192, 128
+    extra = 2 * B * N * D * 4
+    code, ws = _native.accumulate_x_code(lib, torch.float32, B, N, K, D, 4 * extra, 0.25)
+    assert code == _native.FK_F32_XSPLIT
+    assert ws == lib.fk_assign_accumulate_workspace_size(B, N, K, D, _native.FK_F32_XSPLIT)
+    code, ws = _native.accumulate_x_code(lib, torch.float32, B, N, K, D, 2 * extra, 0.25)
+    assert code == _native.FK_F32
+    assert ws == lib.fk_assign_accumulate_workspace_size(B, N, K, D, _native.FK_F32)
+    code, _ = _native.accumulate_x_code(lib, torch.float32, 1, 262144, 1024, 2048, 1 << 40, 0.5)
+    assert code == _native.FK_F32                       # D above XSPLIT_MAX_D
+    code, ws = _native.accumulate_x_code(lib, torch.float16, B, N, K, D, 1 << 40, 0.5)
+    assert code == _native.FK_F16
+    assert ws == lib.fk_assign_accumulate_workspace_size(B, N, K, D, _native.FK_F16)
